@@ -1,0 +1,556 @@
+// FlashAttention-2 forward for B200 (sm_100a), head_dim 64, fp16 in/out.
+//
+// Same mathematics as the reference kernels flash_attn2_wmma_br64/br128
+// (thebigblender/FlashLite csrc/kernel_flash2.cu:54-387, :393-727): scores
+// prescaled by sm_scale*log2(e) (:772), online softmax with base-2
+// exponentials (:232-347), P rounded to fp16 before the PV product while the
+// row sum l accumulates the unrounded fp32 p (:278-294, :339), fully masked
+// rows produce 0 (:364-365). The implementation is a new design:
+//
+//  * one CTA owns one or two 128-row query tiles (Q0, Q1) of one (b,h) slice
+//    and streams 128-key K/V tiles through a 3-stage TMA pipeline into
+//    128B-swizzled shared memory;
+//  * warp 0 issues TMA, warp 1 issues tcgen05.mma from a single thread;
+//    S = Q K^T and O += P V accumulate in Tensor Memory (TMEM), P is written
+//    by the softmax warps straight into TMEM and fed to the MMA as operand A;
+//  * warpgroups 1 and 2 run the online softmax of Q0 and Q1, one thread per
+//    query row (no shuffles), ping-ponging against the tensor core: while one
+//    warpgroup exponentiates, the MMA warp runs the other tile's GEMMs;
+//  * O is rescaled only when a row maximum grows by more than 2^8 (the
+//    result is identical up to rounding: O and l always share one reference
+//    maximum), which removes almost every TMEM round trip of O;
+//  * the epilogue normalises O, stages it in shared memory (reusing the Q
+//    tile) and writes it with one TMA store per tile (coalesced, 16 KB).
+//  * every mbarrier wait is bounded; on timeout the CTA records an error,
+//    drains its in-flight copies and MMAs, frees TMEM and returns.
+//
+// A "merge" instantiation serves ring attention: queries and keys carry
+// global position offsets for the causal mask, and the epilogue merges the
+// block result into a running (fp32 O, log-sum-exp) state in global memory.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "fl_internal.h"
+#include "fl_ptx.cuh"
+
+namespace fl {
+namespace {
+
+constexpr int kBM = 128;      // query rows per tile (UMMA M)
+constexpr int kBN = 128;      // keys per KV tile (UMMA N of S = Q K^T)
+constexpr int kD = 64;        // head dimension
+constexpr int kStages = 3;    // K/V pipeline depth
+constexpr int kThreads = 384; // 3 warpgroups
+constexpr int kTileBytes = kBM * kD * 2;  // 16 KB, one 128x64 fp16 tile
+
+// Tensor Memory columns (512 allocated: the CTA owns the whole SM's TMEM).
+constexpr uint32_t kTmemCols = 512;
+__host__ __device__ constexpr uint32_t col_s(int i) { return i ? 128u : 0u; }   // S, 128 fp32 cols
+__host__ __device__ constexpr uint32_t col_o(int i) { return i ? 320u : 256u; } // O, 64 fp32 cols
+__host__ __device__ constexpr uint32_t col_p(int i) { return i ? 448u : 384u; } // P, 128 fp16 = 64 cols
+
+// A row maximum may exceed the reference maximum by up to this much (log2
+// units) before O and l are rescaled: p <= 2^8 stays exact enough in fp16.
+constexpr float kRescaleThreshold = 8.0f;
+
+// Shared-memory map (offsets from a 1024-byte aligned base).
+constexpr int kSmemQ = 0;                                  // 2 tiles
+constexpr int kSmemK = kSmemQ + 2 * kTileBytes;            // kStages tiles
+constexpr int kSmemV = kSmemK + kStages * kTileBytes;      // kStages tiles
+constexpr int kSmemBar = kSmemV + kStages * kTileBytes;    // mbarriers
+constexpr int kNumBars = 1 + 3 * kStages + 3 * 2 + 1;      // q, k/v/empty, s/p/o, drain
+constexpr int kSmemMisc = kSmemBar + kNumBars * 8;         // tmem base, abort flag
+constexpr int kSmemBytes = kSmemMisc + 16;
+constexpr int kSmemAlloc = kSmemBytes + 1024;              // alignment slack
+
+struct Flash2Params {
+  CUtensorMap tm_q;  // {64, Nq, BH} fp16, box {64, 128, 1}, SW128
+  CUtensorMap tm_k;  // {64, Nk, BH}
+  CUtensorMap tm_v;  // {64, Nk, BH}
+  CUtensorMap tm_o;  // {64, Nq, BH} (unused in merge mode)
+  float* o_acc;      // merge mode: [BH, Nq, 64] fp32
+  float* lse;        // merge mode: [BH, Nq] fp32 (natural log)
+  unsigned int* err; // device error word
+  int nq, nk;        // query / key rows per slice
+  int bh;            // number of (b,h) slices
+  int n_qtiles;      // ceil(nq / 128)
+  int n_ktiles;      // ceil(nk / 128)
+  int tiles_per_cta; // 1 or 2 query tiles per CTA
+  int n_cta_m;       // ceil(n_qtiles / tiles_per_cta)
+  long long q_offset, kv_offset;  // global positions of row 0 (causal mask)
+  float scale_log2;  // sm_scale * log2(e)
+  int first;         // merge mode: overwrite instead of merge
+};
+
+// Number of KV tiles a query tile starting at row q_start must visit.
+__device__ __forceinline__ int kv_tiles_for(const Flash2Params& p, bool causal, int q_start) {
+  if (!causal) return p.n_ktiles;
+  // last visible key position for the tile's last row
+  const long long last = p.q_offset + q_start + kBM - 1 - p.kv_offset;
+  if (last < 0) return 0;
+  const long long t = last / kBN + 1;
+  return t < p.n_ktiles ? static_cast<int>(t) : p.n_ktiles;
+}
+
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int* err) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <bool kCausal, bool kMerge>
+__global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_constant__ Flash2Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t s_q[2] = {sbase + kSmemQ, sbase + kSmemQ + kTileBytes};
+  auto s_k = [&](int st) { return sbase + kSmemK + st * kTileBytes; };
+  auto s_v = [&](int st) { return sbase + kSmemV + st * kTileBytes; };
+  const uint32_t bar0 = sbase + kSmemBar;
+  const uint32_t bar_q = bar0;
+  auto bar_k = [&](int st) { return bar0 + 8u * (1 + st); };
+  auto bar_v = [&](int st) { return bar0 + 8u * (1 + kStages + st); };
+  auto bar_empty = [&](int st) { return bar0 + 8u * (1 + 2 * kStages + st); };
+  auto bar_s = [&](int i) { return bar0 + 8u * (1 + 3 * kStages + i); };
+  auto bar_p = [&](int i) { return bar0 + 8u * (3 + 3 * kStages + i); };
+  auto bar_o = [&](int i) { return bar0 + 8u * (5 + 3 * kStages + i); };
+  const uint32_t bar_drain = bar0 + 8u * (7 + 3 * kStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- work unit: (cta_m, bh); causal launches the longest rows first ----
+  const int lin = blockIdx.x;
+  int cta_m, bh;
+  if (kCausal) {
+    cta_m = p.n_cta_m - 1 - lin / p.bh;
+    bh = lin % p.bh;
+  } else {
+    cta_m = lin % p.n_cta_m;
+    bh = lin / p.n_cta_m;
+  }
+  const int qt0 = cta_m * p.tiles_per_cta;
+  const bool has_q1 = (p.tiles_per_cta == 2) && (qt0 + 1 < p.n_qtiles);
+  const int nkv0 = kv_tiles_for(p, kCausal, qt0 * kBM);
+  const int nkv1 = has_q1 ? kv_tiles_for(p, kCausal, (qt0 + 1) * kBM) : 0;
+  const int nkv = nkv0 > nkv1 ? nkv0 : nkv1;
+
+  // ---- setup ----
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(bar_k(st), 1);
+      mbar_init(bar_v(st), 1);
+      mbar_init(bar_empty(st), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_s(i), 1);
+      mbar_init(bar_p(i), 4);  // one arrival per softmax warp
+      mbar_init(bar_o(i), 1);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Register split: warpgroup 0 (TMA, MMA, two idle warps) gives registers
+  // to the softmax warpgroups. Each role's code sits inside the branch of its
+  // own setmaxnreg so the compiler allocates it against that budget
+  // (128*64 + 256*216 <= 384*168, the launch total).
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n");
+  if (warp == 0) {
+    // ======================= TMA producer =======================
+    int issued = 0;
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_q);
+      tma_prefetch_desc(&p.tm_k);
+      tma_prefetch_desc(&p.tm_v);
+      mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kTileBytes);
+      tma_load_3d(s_q[0], &p.tm_q, bar_q, 0, qt0 * kBM, bh);
+      if (has_q1) tma_load_3d(s_q[1], &p.tm_q, bar_q, 0, (qt0 + 1) * kBM, bh);
+    }
+    __syncwarp();
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j % kStages;
+      const uint32_t ph = (j / kStages) & 1;
+      if (!warp_wait(bar_empty(st), ph ^ 1, abort_flag, p.err)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_k(st), kTileBytes);
+        tma_load_3d(s_k(st), &p.tm_k, bar_k(st), 0, j * kBN, bh);
+        mbar_arrive_expect_tx(bar_v(st), kTileBytes);
+        tma_load_3d(s_v(st), &p.tm_v, bar_v(st), 0, j * kBN, bh);
+      }
+      __syncwarp();
+      issued = j + 1;
+    }
+    if (*abort_flag && lane == 0) {
+      // Drain: let every copy this CTA started land before shared memory is released.
+      mbar_wait_quiet(bar_q, 0);
+      for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
+        mbar_wait_quiet(bar_k(j % kStages), (j / kStages) & 1);
+        mbar_wait_quiet(bar_v(j % kStages), (j / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer =======================
+    constexpr uint32_t idesc_s = make_idesc_f16_f32(kBM, kBN, false);  // K-major A and B
+    constexpr uint32_t idesc_pv = make_idesc_f16_f32(kBM, kD, true);   // B (= V) MN-major
+    const bool leader = (lane == 0);
+    auto issue_s = [&](int i, int st) {
+      if (leader) {
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t a = make_sdesc_sw128(s_q[i] + kk * 32, 16, 1024);
+          const uint64_t b = make_sdesc_sw128(s_k(st) + kk * 32, 16, 1024);
+          umma_f16_ss(tmem + col_s(i), a, b, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_s(i));
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int i, int st, int j, bool last) {
+      if (leader) {
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t b = make_sdesc_sw128(s_v(st) + kk * 16 * kD * 2, 8192, 1024);
+          umma_f16_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (last) umma_commit(bar_o(i));
+      }
+      __syncwarp();
+    };
+
+    bool ok = warp_wait(bar_q, 0, abort_flag, p.err);
+    if (ok) ok = warp_wait(bar_k(0), 0, abort_flag, p.err);
+    if (ok) {
+      tc_fence_after();
+      if (nkv0 > 0) issue_s(0, 0);
+      if (nkv1 > 0) issue_s(1, 0);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j % kStages;
+        if (!warp_wait(bar_v(st), (j / kStages) & 1, abort_flag, p.err)) break;
+        if (j < nkv0) {
+          if (!warp_wait(bar_p(0), j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+          issue_pv(0, st, j, j == nkv0 - 1);
+        }
+        const int st1 = (j + 1) % kStages;
+        if (j + 1 < nkv) {
+          if (!warp_wait(bar_k(st1), ((j + 1) / kStages) & 1, abort_flag, p.err)) break;
+        }
+        if (j + 1 < nkv0) issue_s(0, st1);
+        if (j < nkv1) {
+          if (!warp_wait(bar_p(1), j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+          issue_pv(1, st, j, j == nkv1 - 1);
+        }
+        if (j + 1 < nkv1) issue_s(1, st1);
+        if (leader) umma_commit(bar_empty(st));
+        __syncwarp();
+      }
+    }
+    // Drain: wait until every MMA this thread issued has completed.
+    if (leader) {
+      umma_commit(bar_drain);
+      mbar_wait_quiet(bar_drain, 0);
+    }
+    __syncwarp();
+  }
+  // warps 2 and 3 have no role in this design.
+  } else {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n");
+  {
+    // ======================= softmax warpgroups =======================
+    const int i = (warp - 4) >> 2;               // query tile handled: 0 or 1
+    const int t = threadIdx.x - 128 * (1 + i);   // row within the tile
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t tS = tmem + lane_base + col_s(i);
+    const uint32_t tP = tmem + lane_base + col_p(i);
+    const uint32_t tO = tmem + lane_base + col_o(i);
+    const int q_start = (qt0 + i) * kBM;
+    const int my_nkv = (i == 0) ? nkv0 : nkv1;
+    const bool active = (i == 0) || has_q1;
+
+    float sc = p.scale_log2;
+    const bool prescale = !(sc > 0.0f);  // negative scales: scale before max/mask
+    float m_ref = -INFINITY;
+    float l = 0.0f;
+    bool ok = true;
+
+    for (int j = 0; j < my_nkv; ++j) {
+      if (!warp_wait(bar_s(i), j & 1, abort_flag, p.err)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld128_wait(tS, sr);
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
+      float scl = sc;
+      if (prescale) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] *= sc;
+        scl = 1.0f;
+      }
+      const int k_start = j * kBN;
+      // keys visible to this row: c < limit
+      long long lim = p.nk - k_start;
+      if (kCausal) {
+        const long long d = p.q_offset + q_start + t - (p.kv_offset + k_start) + 1;
+        lim = d < lim ? d : lim;
+      }
+      if (lim < kBN) {
+        const int limit = lim < 0 ? 0 : static_cast<int>(lim);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      const float m_tile = mx * scl;
+      const float m_new = fmaxf(m_ref, m_tile);
+      const bool need = m_new > m_ref + kRescaleThreshold;
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2_approx(m_ref - m_new);
+        m_ref = m_new;
+      }
+      l *= alpha;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // PV of the previous tile has completed: the commit behind bar_s(i)
+        // tracks every MMA issued before this tile's S.
+        uint32_t o[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tmem_ld32_wait(tO + h * 32, o);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st32(tO + h * 32, o);
+        }
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int c = q * 32 + 2 * e;
+          const float p0 = ex2_approx(fmaf(s[c], scl, -m_use));
+          const float p1 = ex2_approx(fmaf(s[c + 1], scl, -m_use));
+          l += p0 + p1;
+          pk[e] = pack_f16x2(p0, p1);
+        }
+        tmem_st16(tP + q * 16, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p(i));
+    }
+
+    // ---- epilogue ----
+    if (active && my_nkv > 0 && ok) ok = warp_wait(bar_o(i), 0, abort_flag, p.err);
+    const bool do_out = active && my_nkv > 0 && ok;
+    uint32_t o[64];
+    if (do_out) {
+      tc_fence_after();
+      uint32_t tmp[32];
+      tmem_ld32_wait(tO, tmp);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = tmp[c];
+      tmem_ld32_wait(tO + 32, tmp);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[32 + c] = tmp[c];
+    }
+    const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
+    if (!kMerge) {
+      if (do_out) {
+        // Stage the fp16 tile in the (now unused) Q buffer with the 128B
+        // swizzle the TMA store expects: 16-byte chunk c of row t goes to
+        // chunk position c ^ (t % 8).
+        uint8_t* row = smem + kSmemQ + i * kTileBytes + t * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 v;
+          v.x = pack_f16x2(__uint_as_float(o[8 * c + 0]) * inv_l, __uint_as_float(o[8 * c + 1]) * inv_l);
+          v.y = pack_f16x2(__uint_as_float(o[8 * c + 2]) * inv_l, __uint_as_float(o[8 * c + 3]) * inv_l);
+          v.z = pack_f16x2(__uint_as_float(o[8 * c + 4]) * inv_l, __uint_as_float(o[8 * c + 5]) * inv_l);
+          v.w = pack_f16x2(__uint_as_float(o[8 * c + 6]) * inv_l, __uint_as_float(o[8 * c + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(row + ((c ^ (t & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+      }
+      named_bar_sync(1 + i, 128);
+      if (do_out && t == 0 && !*abort_flag) {
+        tma_store_3d(&p.tm_o, s_q[i], 0, q_start, bh);
+        tma_store_commit();
+        tma_store_wait_read0();
+      }
+    } else {
+      const int row = q_start + t;
+      if (active && row < p.nq && (do_out || (p.first && my_nkv == 0 && ok))) {
+        // ln(sum_j exp(s_j*scale)) = (m_ref + log2(l)) * ln(2)
+        const float lse_blk = (l > 0.0f) ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
+        float* orow = p.o_acc + (static_cast<long long>(bh) * p.nq + row) * kD;
+        float* lrow = p.lse + static_cast<long long>(bh) * p.nq + row;
+        float w_old = 0.0f, w_new = 1.0f, lse_out = lse_blk;
+        if (!p.first) {
+          const float lse_old = *lrow;
+          const float mx = fmaxf(lse_old, lse_blk);
+          if (mx == -INFINITY) {
+            w_old = 0.0f; w_new = 0.0f; lse_out = -INFINITY;
+          } else {
+            const float a = __expf(lse_old - mx), b = __expf(lse_blk - mx);
+            const float sum = a + b;
+            w_old = a / sum; w_new = b / sum;
+            lse_out = mx + __logf(sum);
+          }
+        } else if (lse_blk == -INFINITY) {
+          w_new = 0.0f;
+        }
+        const float wn = w_new * inv_l;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float4 r;
+          const float o0 = do_out ? __uint_as_float(o[4 * c + 0]) : 0.0f;
+          const float o1 = do_out ? __uint_as_float(o[4 * c + 1]) : 0.0f;
+          const float o2 = do_out ? __uint_as_float(o[4 * c + 2]) : 0.0f;
+          const float o3 = do_out ? __uint_as_float(o[4 * c + 3]) : 0.0f;
+          if (p.first) {
+            r = make_float4(o0 * wn, o1 * wn, o2 * wn, o3 * wn);
+          } else {
+            const float4 prev = reinterpret_cast<const float4*>(orow)[c];
+            r = make_float4(prev.x * w_old + o0 * wn, prev.y * w_old + o1 * wn,
+                            prev.z * w_old + o2 * wn, prev.w * w_old + o3 * wn);
+          }
+          reinterpret_cast<float4*>(orow)[c] = r;
+        }
+        *lrow = lse_out;
+      }
+    }
+  }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+// Tensor map over a [slices, rows, 64] fp16 array with a {64, 128, 1} box.
+bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t slices) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(slices)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD * 2),
+                           static_cast<cuuint64_t>(rows) * kD * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kBM), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool kCausal, bool kMerge>
+cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t stream) {
+  auto kern = flash2_fwd_kernel<kCausal, kMerge>;
+  static int configured_mask = 0;  // bit per device (up to 32 devices)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured_mask & (1 << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+    if (e != cudaSuccess) return e;
+    configured_mask |= (1 << (dev & 31));
+  }
+  kern<<<grid, kThreads, kSmemAlloc, stream>>>(prm);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
+                          float* lse, int64_t BH, int64_t Nq, int64_t Nk, int64_t q_offset,
+                          int64_t kv_offset, float scale_log2, bool causal, bool merge,
+                          bool first, cudaStream_t stream) {
+  Flash2Params prm;
+  if (!encode_rows_map(&prm.tm_q, q, Nq, BH) || !encode_rows_map(&prm.tm_k, k, Nk, BH) ||
+      !encode_rows_map(&prm.tm_v, v, Nk, BH)) {
+    return cudaErrorInvalidValue;
+  }
+  if (!merge) {
+    if (!encode_rows_map(&prm.tm_o, o_f16, Nq, BH)) return cudaErrorInvalidValue;
+  } else {
+    prm.tm_o = prm.tm_q;
+  }
+  prm.o_acc = o_acc;
+  prm.lse = lse;
+  prm.err = device_error_word();
+  prm.nq = static_cast<int>(Nq);
+  prm.nk = static_cast<int>(Nk);
+  prm.bh = static_cast<int>(BH);
+  prm.n_qtiles = static_cast<int>((Nq + kBM - 1) / kBM);
+  prm.n_ktiles = static_cast<int>((Nk + kBN - 1) / kBN);
+  const int64_t pairs = (prm.n_qtiles + 1) / 2;
+  // Two query tiles per CTA keep the tensor core busy while one tile is in
+  // softmax; fall back to one tile per CTA when that would leave SMs idle.
+  prm.tiles_per_cta = (pairs * BH >= sm_count()) ? 2 : 1;
+  prm.n_cta_m = (prm.n_qtiles + prm.tiles_per_cta - 1) / prm.tiles_per_cta;
+  prm.q_offset = q_offset;
+  prm.kv_offset = kv_offset;
+  prm.scale_log2 = scale_log2;
+  prm.first = first ? 1 : 0;
+  const int64_t grid = static_cast<int64_t>(prm.n_cta_m) * BH;
+  if (grid <= 0 || grid > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (merge) {
+    return causal ? launch_variant<true, true>(prm, static_cast<int>(grid), stream)
+                  : launch_variant<false, true>(prm, static_cast<int>(grid), stream);
+  }
+  return causal ? launch_variant<true, false>(prm, static_cast<int>(grid), stream)
+                : launch_variant<false, false>(prm, static_cast<int>(grid), stream);
+}
+
+}  // namespace fl

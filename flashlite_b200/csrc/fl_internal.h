@@ -1,0 +1,31 @@
+// Internal (host-side) declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+
+namespace fl {
+
+// Per-thread text of the last error; returned by fl_last_error().
+void set_last_error(const std::string& msg);
+const char* last_error();
+
+// Device-side error word of the current device (address in device memory).
+unsigned int* device_error_word();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Launchers. All sizes validated by the caller; return 0 or a cudaError_t.
+cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
+                          float* lse, int64_t BH, int64_t Nq, int64_t Nk, int64_t q_offset,
+                          int64_t kv_offset, float scale_log2, bool causal, bool merge,
+                          bool first, cudaStream_t stream);
+
+cudaError_t launch_naive(const void* q, const void* k, const void* v, void* o, int64_t BH,
+                         int64_t N, int64_t D, float sm_scale, bool causal, cudaStream_t stream);
+
+cudaError_t launch_ring_finalize(const float* o_acc, void* o, int64_t n, cudaStream_t stream);
+
+}  // namespace fl

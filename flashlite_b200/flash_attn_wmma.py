@@ -1,0 +1,25 @@
+"""Drop-in replacement of the reference module ``flash_attn_wmma``.
+
+Same functions, argument names, defaults and error behaviour as
+thebigblender/FlashLite ``csrc/flash_attn.cpp:4-29``:
+
+* ``forward_flash2(q, k, v, sm_scale=0.0, is_causal=False, out=None)``
+  FlashAttention-2 forward on ``[B, H, N, 64]`` fp16 CUDA tensors. With
+  ``out`` given, the result is written there and ``out`` is returned (the
+  zero-allocation form). ``sm_scale == 0`` means ``1/sqrt(D)``.
+* ``forward_naive(q, k, v, sm_scale=0.0, is_causal=False)``
+  unfused CUDA-core baseline, any head_dim up to 1024.
+
+Invalid inputs raise ``RuntimeError`` with the reference's messages. The
+functions are the C++ binding's own (``flashlite_b200._C``); there is no
+Python or CPU fallback.
+
+Extra entry points (no reference counterpart) used by ring attention:
+``forward_block`` and ``ring_finalize``; ``device_error`` reads the error
+bits kernels raise when a bounded wait gives up.
+"""
+from __future__ import annotations
+
+from ._C import device_error, forward_block, forward_flash2, forward_naive, ring_finalize
+
+__all__ = ["forward_flash2", "forward_naive", "forward_block", "ring_finalize", "device_error"]

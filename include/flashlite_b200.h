@@ -1,0 +1,95 @@
+/*
+ * flashlite_b200 — C ABI of the B200 (sm_100a) FlashAttention-2 forward engine.
+ *
+ * Plain pointers and sizes only: no torch, no C++ types. Every tensor is a
+ * contiguous fp16 array laid out [B, H, N, D] (element (b,h,n,d) at offset
+ * ((b*H + h)*N + n)*D + d), resident in device memory of the current device.
+ * Calls are asynchronous on `stream` (a cudaStream_t passed as void*; NULL =
+ * the legacy default stream) and return a status code; a non-zero status
+ * means nothing was launched. Errors found by a kernel while it runs (a
+ * bounded wait that gave up) are reported by fl_device_error().
+ *
+ * Reference interface being replaced (thebigblender/FlashLite):
+ *   csrc/includes/flash_attn.h:100-124   host declarations
+ *   csrc/flash_attn.cpp:4-29             pybind11 module `flash_attn_wmma`
+ */
+#ifndef FLASHLITE_B200_H_
+#define FLASHLITE_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+typedef enum fl_status {
+  FL_OK = 0,
+  FL_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, size overflow      */
+  FL_ERR_UNSUPPORTED = 2,      /* e.g. head_dim != 64 for the FA2 kernel       */
+  FL_ERR_MISALIGNED = 3,       /* a pointer is not 16-byte aligned             */
+  FL_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed            */
+  FL_ERR_NO_DEVICE = 5,        /* current device is not sm_100 (B200 class)    */
+  FL_ERR_DEVICE_TIMEOUT = 6    /* a kernel's bounded wait gave up (see below)  */
+} fl_status;
+
+/*
+ * FlashAttention-2 forward: o = softmax(q k^T * sm_scale [causal]) v.
+ * Replaces flash_attn::flash_attn_forward_flash2 (csrc/kernel_flash2.cu:732-839).
+ * q, k, v, o: [B, H, N, D] fp16, D must be 64 (csrc/kernel_flash2.cu:756-757).
+ * sm_scale == 0 selects 1/sqrt(D) (csrc/kernel_flash2.cu:769-771).
+ * is_causal != 0 masks keys j > query i. o may not alias q, k or v.
+ */
+int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
+                  int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);
+
+/*
+ * Naive (unfused, fp32 CUDA-core) attention forward, any D in [1, 1024].
+ * Replaces flash_attn::flash_attn_forward_naive (csrc/kernel_naive.cu:242-323).
+ */
+int fl_naive_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
+                 int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);
+
+/*
+ * One block step of sequence-sharded (ring) attention; no reference
+ * counterpart (the reference is single-GPU). Attends the query block q
+ * [BH, Nq, 64] (global positions q_offset..q_offset+Nq-1) to the key/value
+ * block k, v [BH, Nk, 64] (positions kv_offset..), causal by global position
+ * when is_causal != 0, and merges the result into the running state:
+ *   o_acc  [BH, Nq, 64] fp32, normalised partial output
+ *   lse    [BH, Nq]     fp32, natural-log sum-exp of the scaled scores
+ * If `first` != 0 the running state is overwritten instead of merged.
+ * Rows with no visible key keep (o_acc, lse) = (0, -inf) when `first`.
+ */
+int fl_flash2_fwd_block(const void* q, const void* k, const void* v, float* o_acc, float* lse,
+                        int64_t BH, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
+                        int64_t kv_offset, float sm_scale, int is_causal, int first,
+                        void* stream);
+
+/*
+ * Final step of ring attention: o[i] = fp16(o_acc[i]) for BH*Nq*D elements.
+ * No reference counterpart.
+ */
+int fl_ring_finalize(const float* o_acc, void* o, int64_t n_elems, void* stream);
+
+/* Human-readable text for a status code (static storage). */
+const char* fl_status_str(int status);
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* fl_last_error(void);
+
+/*
+ * Reads and clears the device error word of the current device after
+ * synchronising `stream`. Writes the raw bit flags to *flags (may be NULL)
+ * and returns FL_ERR_DEVICE_TIMEOUT if any kernel gave up a wait, else FL_OK.
+ */
+int fl_device_error(void* stream, uint32_t* flags);
+
+/* Library version as "major.minor.patch". */
+const char* fl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHLITE_B200_H_ */

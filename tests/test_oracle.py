@@ -1,0 +1,114 @@
+"""CPU tests: pin the oracle before trusting it.
+
+1. Against torch SDPA, the oracle the reference's own tests use
+   (thebigblender/FlashLite tests/test_correctness.py:43-45, 75-77), over the
+   reference's test matrix (:29-33, :61-65) at its tolerance (:58, :90).
+2. Against the committed golden vectors (tests/golden/, made by
+   tests/golden/make_golden.py).
+3. The restatement of the reference kernel's tiled numerics meets the
+   north-star tolerance against the exact oracle (so the tolerance is one the
+   reference itself satisfies).
+4. Block/LSE merge identities used by ring attention.
+"""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import attention_oracle as orc
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("batch_size", [1, 2])
+@pytest.mark.parametrize("num_heads", [4, 8])
+@pytest.mark.parametrize("seq_len", [128, 256, 512])
+@pytest.mark.parametrize("is_causal", [False, True])
+def test_oracle_matches_sdpa_reference_matrix(batch_size, num_heads, seq_len, is_causal):
+    q, k, v = orc.make_qkv(batch_size, num_heads, seq_len, 64, seed=42)
+    scale = 1.0 / math.sqrt(64)
+    ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=is_causal,
+                                         scale=scale)
+    out = orc.attention_fp32(q, k, v, scale, is_causal)
+    torch.testing.assert_close(out, ref, rtol=1e-3, atol=1e-3)
+    mx, _ = orc.error_metrics(out, ref)
+    assert mx < 1e-5
+
+
+def test_default_scale_is_inverse_sqrt_d():
+    q, k, v = orc.make_qkv(1, 2, 64, 64, seed=1)
+    a = orc.attention_fp32(q, k, v, 0.0, False)
+    b = orc.attention_fp32(q, k, v, 1.0 / math.sqrt(64), False)
+    torch.testing.assert_close(a, b, rtol=0, atol=1e-6)
+
+
+def test_flops_formula():
+    # benchmarks/benchmark_throughput.py:23-31
+    assert orc.flops(2, 8, 4096, 64, False) == 4 * 2 * 8 * 4096 ** 2 * 64
+    assert orc.flops(2, 8, 4096, 64, True) == 2 * 2 * 8 * 4096 ** 2 * 64
+
+
+def test_make_qkv_is_shard_independent():
+    q, k, v = orc.make_qkv(2, 3, 16, 8, seed=7)
+    qs, ks, vs = orc.make_qkv(2, 3, 16, 8, seed=7, slices=range(2, 5))
+    assert torch.equal(q.view(6, 16, 8)[2:5], qs.view(3, 16, 8))
+    assert torch.equal(v.view(6, 16, 8)[2:5], vs.view(3, 16, 8))
+
+
+def _golden_files():
+    return sorted(GOLDEN.glob("golden_*.npz"))
+
+
+def test_golden_files_present():
+    assert len(_golden_files()) >= 4
+
+
+@pytest.mark.parametrize("path", _golden_files(), ids=lambda p: p.stem)
+def test_oracle_matches_golden(path):
+    g = np.load(path)
+    q, k, v = (torch.from_numpy(g[n]) for n in ("q", "k", "v"))
+    out = orc.attention_fp32(q, k, v, float(g["sm_scale"]), bool(g["is_causal"]))
+    np.testing.assert_allclose(out.numpy(), g["out_fp32"], rtol=0, atol=2e-6)
+    # inputs are regenerated bit-exactly from the seed
+    B, H, N, D = q.shape
+    q2, _, _ = orc.make_qkv(B, H, N, D, seed=int(g["seed"]), scale=float(g["input_scale"]))
+    assert torch.equal(q2, q)
+
+
+@pytest.mark.parametrize("N,causal", [(128, False), (200, True), (256, True), (1000, False)])
+def test_reference_tiled_numerics_meet_tolerance(N, causal):
+    q, k, v = orc.make_qkv(1, 2, N, 64, seed=3)
+    ref = orc.attention_fp32(q, k, v, 0.125, causal)
+    tiled = torch.from_numpy(orc.flash2_tiled_reference(q, k, v, 0.125, causal))
+    mx, mean = orc.error_metrics(tiled, ref)
+    assert mx <= orc.MAX_ABS_TOL and mean <= orc.MEAN_ABS_TOL, (mx, mean)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_block_merge_equals_full_attention(causal):
+    torch.manual_seed(0)
+    N, P = 96, 3
+    q, k, v = orc.make_qkv(1, 2, N, 16, seed=5)
+    q, k, v = (t.view(2, N, 16) for t in (q, k, v))
+    full = orc.attention_fp32(q, k, v, 0.25, causal)
+    nb = N // P
+    for r in range(P):
+        qb = q[:, r * nb:(r + 1) * nb]
+        o, lse = None, None
+        for s in range(P):
+            kb, vb = k[:, s * nb:(s + 1) * nb], v[:, s * nb:(s + 1) * nb]
+            ob, lb = orc.block_attention_lse(qb, kb, vb, r * nb, s * nb, 0.25, causal)
+            o, lse = (ob, lb) if o is None else orc.merge_lse(o, lse, ob, lb)
+        torch.testing.assert_close(o, full[:, r * nb:(r + 1) * nb], rtol=1e-5, atol=1e-5)
+
+
+def test_rows_oracle_matches_full():
+    q, k, v = orc.make_qkv(1, 2, 300, 64, seed=9)
+    full = orc.attention_fp32(q, k, v, 0.125, True).view(2, 300, 64)
+    rows = torch.tensor([0, 1, 127, 128, 299])
+    part = orc.attention_rows_fp32(q.view(2, 300, 64), k.view(2, 300, 64), v.view(2, 300, 64),
+                                   rows, 0.125, True)
+    torch.testing.assert_close(part, full[:, rows], rtol=1e-6, atol=1e-6)
