@@ -4,21 +4,26 @@
 // (thebigblender/FlashLite csrc/kernel_flash2.cu:54-387, :393-727): scores
 // prescaled by sm_scale*log2(e) (:772), online softmax with base-2
 // exponentials (:232-347), P rounded to fp16 before the PV product while the
-// row sum l accumulates the unrounded fp32 p (:278-294, :339), fully masked
-// rows produce 0 (:364-365). The implementation is a new design:
+// row sum l accumulates fp32 p (:278-294, :339), fully masked rows produce 0
+// (:364-365). The implementation is a new design:
 //
 //  * one CTA owns one or two 128-row query tiles (Q0, Q1) of one (b,h) slice
-//    and streams 128-key K/V tiles through a 3-stage TMA pipeline into
-//    128B-swizzled shared memory;
-//  * warp 0 issues TMA, warp 1 issues tcgen05.mma from a single thread;
-//    S = Q K^T and O += P V accumulate in Tensor Memory (TMEM), P is written
-//    by the softmax warps straight into TMEM and fed to the MMA as operand A;
+//    and streams 128-key K and V tiles through two independent TMA rings
+//    (kStagesK / kStagesV deep, 128B-swizzled shared memory). K and V have
+//    their own producer warps and are released separately (K after the last
+//    S = Q K^T that reads it, V after the last P V), so loads run far ahead
+//    of use: a TMA tile load takes several microseconds to land here.
+//  * warp 1 issues tcgen05.mma from one elected lane with warp-uniform
+//    operands; S and O accumulate in Tensor Memory (TMEM), P is written by
+//    the softmax warps into its own TMEM columns and fed as operand A.
 //  * warpgroups 1 and 2 run the online softmax of Q0 and Q1, one thread per
-//    query row (no shuffles), ping-ponging against the tensor core: while one
-//    warpgroup exponentiates, the MMA warp runs the other tile's GEMMs;
-//  * O is rescaled only when a row maximum grows by more than 2^8 (the
-//    result is identical up to rounding: O and l always share one reference
-//    maximum), which removes almost every TMEM round trip of O;
+//    query row. A softmax warp releases its S columns right after loading
+//    them (barrier s_free), so S_{j+1} = Q K_{j+1}^T runs on the tensor core
+//    while tile j is still being exponentiated; the only wait left on the
+//    softmax path is for P V of the previous tile (its P columns are reused).
+//  * O is rescaled only when a row maximum grows by more than 2^8 (O and l
+//    always share one reference maximum, so the result is unchanged up to
+//    rounding), which removes almost every TMEM round trip of O.
 //  * the epilogue normalises O, stages it in shared memory (reusing the Q
 //    tile) and writes it with one TMA store per tile (coalesced, 16 KB).
 //  * every mbarrier wait is bounded; on timeout the CTA records an error,
@@ -42,11 +47,12 @@
 namespace fl {
 namespace {
 
-constexpr int kBM = 128;      // query rows per tile (UMMA M)
-constexpr int kBN = 128;      // keys per KV tile (UMMA N of S = Q K^T)
-constexpr int kD = 64;        // head dimension
-constexpr int kStages = 3;    // K/V pipeline depth
-constexpr int kThreads = 384; // 3 warpgroups
+constexpr int kBM = 128;       // query rows per tile (UMMA M)
+constexpr int kBN = 128;       // keys per KV tile (UMMA N of S = Q K^T)
+constexpr int kD = 64;         // head dimension
+constexpr int kStagesK = 4;    // K ring depth
+constexpr int kStagesV = 4;    // V ring depth
+constexpr int kThreads = 384;  // 3 warpgroups
 constexpr int kTileBytes = kBM * kD * 2;  // 16 KB, one 128x64 fp16 tile
 
 // Tensor Memory columns (512 allocated: the CTA owns the whole SM's TMEM).
@@ -59,12 +65,22 @@ __host__ __device__ constexpr uint32_t col_p(int i) { return i ? 448u : 384u; } 
 // units) before O and l are rescaled: p <= 2^8 stays exact enough in fp16.
 constexpr float kRescaleThreshold = 8.0f;
 
+// Bit e set: column pair e (mod 8) of every 16-column group is exponentiated
+// on the FMA pipe (exp2_poly2) instead of the MUFU (3 of 8 pairs).
+#ifndef FL_POLY_PAIRS
+#define FL_POLY_PAIRS 0x92
+#endif
+constexpr unsigned kPolyPairs = FL_POLY_PAIRS;
+static_assert(__builtin_popcount(kPolyPairs & 0xff) == 3,
+              "the split row-max below assumes 3 of 8 column pairs on the FMA pipe");
+
 // Shared-memory map (offsets from a 1024-byte aligned base).
 constexpr int kSmemQ = 0;                                  // 2 tiles
-constexpr int kSmemK = kSmemQ + 2 * kTileBytes;            // kStages tiles
-constexpr int kSmemV = kSmemK + kStages * kTileBytes;      // kStages tiles
-constexpr int kSmemBar = kSmemV + kStages * kTileBytes;    // mbarriers
-constexpr int kNumBars = 1 + 3 * kStages + 3 * 2 + 1;      // q, k/v/empty, s/p/o, drain
+constexpr int kSmemK = kSmemQ + 2 * kTileBytes;            // kStagesK tiles
+constexpr int kSmemV = kSmemK + kStagesK * kTileBytes;     // kStagesV tiles
+constexpr int kSmemBar = kSmemV + kStagesV * kTileBytes;   // mbarriers
+// q | k full/empty | v full/empty | s_full, s_free, p_full, pv_done (x2) | drain
+constexpr int kNumBars = 1 + 2 * kStagesK + 2 * kStagesV + 4 * 2 + 1;
 constexpr int kSmemMisc = kSmemBar + kNumBars * 8;         // tmem base, abort flag
 constexpr int kSmemBytes = kSmemMisc + 16;
 constexpr int kSmemAlloc = kSmemBytes + 1024;              // alignment slack
@@ -104,6 +120,58 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
+// Variant for the MMA-issuing warp: spins without suspending.
+__device__ __forceinline__ bool warp_wait_spin(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, unsigned int* err) {
+  const bool ok = mbar_wait_spin(bar, parity, abort_flag, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Optional phase trace (build with -DFL_TRACE; compiled out otherwise):
+// CTA 0 records clock64() at pipeline events of its first kTraceIters KV
+// tiles into fl_trace_buf[event][iteration] for timeline analysis.
+#ifdef FL_TRACE
+constexpr int kTraceIters = 64;
+constexpr int kTraceEvents = 20;
+__device__ long long fl_trace_buf[kTraceEvents * kTraceIters];
+#define FL_TRACE_EV(ev, it)                                                        \
+  do {                                                                             \
+    if (blockIdx.x == 0 && (it) < kTraceIters)                                     \
+      fl_trace_buf[(ev) * kTraceIters + (it)] = clock64();                         \
+  } while (0)
+#else
+#define FL_TRACE_EV(ev, it) \
+  do {                      \
+  } while (0)
+#endif
+
+// TMA producer of one ring (K or V): tile t goes to stage t % kStages once
+// the consumer released that stage. Returns the number of tiles issued.
+template <int kStages>
+__device__ __forceinline__ int produce_ring(const CUtensorMap* tm, uint32_t s_ring, uint32_t bar_full0,
+                                            uint32_t bar_empty0, int n_tiles, int bh, int lane,
+                                            volatile int* abort_flag, unsigned int* err) {
+  int issued = 0;
+  for (int t = 0; t < n_tiles; ++t) {
+    const int st = t % kStages;
+    const uint32_t ph = (t / kStages) & 1;
+    if (!warp_wait(bar_empty0 + 8u * st, ph ^ 1, abort_flag, err)) break;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar_full0 + 8u * st, kTileBytes);
+      tma_load_3d(s_ring + st * kTileBytes, tm, bar_full0 + 8u * st, 0, t * kBN, bh);
+    }
+    __syncwarp();
+    issued = t + 1;
+  }
+  return issued;
+}
+
+template <int kStages>
+__device__ __forceinline__ void drain_ring(uint32_t bar_full0, int issued) {
+  for (int t = issued > kStages ? issued - kStages : 0; t < issued; ++t)
+    mbar_wait_quiet(bar_full0 + 8u * (t % kStages), (t / kStages) & 1);
+}
+
 template <bool kCausal, bool kMerge>
 __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_constant__ Flash2Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -111,17 +179,23 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t s_q[2] = {sbase + kSmemQ, sbase + kSmemQ + kTileBytes};
-  auto s_k = [&](int st) { return sbase + kSmemK + st * kTileBytes; };
-  auto s_v = [&](int st) { return sbase + kSmemV + st * kTileBytes; };
-  const uint32_t bar0 = sbase + kSmemBar;
-  const uint32_t bar_q = bar0;
-  auto bar_k = [&](int st) { return bar0 + 8u * (1 + st); };
-  auto bar_v = [&](int st) { return bar0 + 8u * (1 + kStages + st); };
-  auto bar_empty = [&](int st) { return bar0 + 8u * (1 + 2 * kStages + st); };
-  auto bar_s = [&](int i) { return bar0 + 8u * (1 + 3 * kStages + i); };
-  auto bar_p = [&](int i) { return bar0 + 8u * (3 + 3 * kStages + i); };
-  auto bar_o = [&](int i) { return bar0 + 8u * (5 + 3 * kStages + i); };
-  const uint32_t bar_drain = bar0 + 8u * (7 + 3 * kStages);
+  const uint32_t s_k0 = sbase + kSmemK;
+  const uint32_t s_v0 = sbase + kSmemV;
+  const uint32_t bar_q = sbase + kSmemBar;
+  const uint32_t bar_kfull0 = bar_q + 8;
+  const uint32_t bar_kempty0 = bar_kfull0 + 8 * kStagesK;
+  const uint32_t bar_vfull0 = bar_kempty0 + 8 * kStagesK;
+  const uint32_t bar_vempty0 = bar_vfull0 + 8 * kStagesV;
+  const uint32_t bar_x0 = bar_vempty0 + 8 * kStagesV;
+  auto bar_kfull = [&](int st) { return bar_kfull0 + 8u * st; };
+  auto bar_kempty = [&](int st) { return bar_kempty0 + 8u * st; };
+  auto bar_vfull = [&](int st) { return bar_vfull0 + 8u * st; };
+  auto bar_vempty = [&](int st) { return bar_vempty0 + 8u * st; };
+  auto bar_s = [&](int i) { return bar_x0 + 8u * (0 + i); };       // S_i ready in TMEM
+  auto bar_sfree = [&](int i) { return bar_x0 + 8u * (2 + i); };   // S_i loaded by softmax
+  auto bar_p = [&](int i) { return bar_x0 + 8u * (4 + i); };       // P_i written
+  auto bar_pv = [&](int i) { return bar_x0 + 8u * (6 + i); };      // P_i V done (O_i updated)
+  const uint32_t bar_drain = bar_x0 + 8u * 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
 
@@ -147,15 +221,19 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   // ---- setup ----
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int st = 0; st < kStages; ++st) {
-      mbar_init(bar_k(st), 1);
-      mbar_init(bar_v(st), 1);
-      mbar_init(bar_empty(st), 1);
+    for (int st = 0; st < kStagesK; ++st) {
+      mbar_init(bar_kfull(st), 1);
+      mbar_init(bar_kempty(st), 1);
+    }
+    for (int st = 0; st < kStagesV; ++st) {
+      mbar_init(bar_vfull(st), 1);
+      mbar_init(bar_vempty(st), 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s(i), 1);
-      mbar_init(bar_p(i), 4);  // one arrival per softmax warp
-      mbar_init(bar_o(i), 1);
+      mbar_init(bar_sfree(i), 4);  // one arrival per softmax warp
+      mbar_init(bar_p(i), 4);
+      mbar_init(bar_pv(i), 1);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -170,112 +248,134 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Register split: warpgroup 0 (TMA, MMA, two idle warps) gives registers
-  // to the softmax warpgroups. Each role's code sits inside the branch of its
-  // own setmaxnreg so the compiler allocates it against that budget
-  // (128*64 + 256*216 <= 384*168, the launch total).
+  // Register split: warpgroup 0 (K producer, MMA, V producer, idle) gives
+  // registers to the softmax warpgroups. Each role's code sits inside the
+  // branch of its own setmaxnreg so the compiler allocates it against that
+  // budget (128*64 + 256*216 <= 384*168, the launch total).
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n");
   if (warp == 0) {
-    // ======================= TMA producer =======================
-    int issued = 0;
+    // ======================= Q + K producer =======================
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_k);
-      tma_prefetch_desc(&p.tm_v);
       mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kTileBytes);
       tma_load_3d(s_q[0], &p.tm_q, bar_q, 0, qt0 * kBM, bh);
       if (has_q1) tma_load_3d(s_q[1], &p.tm_q, bar_q, 0, (qt0 + 1) * kBM, bh);
     }
     __syncwarp();
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j % kStages;
-      const uint32_t ph = (j / kStages) & 1;
-      if (!warp_wait(bar_empty(st), ph ^ 1, abort_flag, p.err)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar_k(st), kTileBytes);
-        tma_load_3d(s_k(st), &p.tm_k, bar_k(st), 0, j * kBN, bh);
-        mbar_arrive_expect_tx(bar_v(st), kTileBytes);
-        tma_load_3d(s_v(st), &p.tm_v, bar_v(st), 0, j * kBN, bh);
-      }
-      __syncwarp();
-      issued = j + 1;
-    }
+    const int issued = produce_ring<kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv, bh,
+                                              lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) {
       // Drain: let every copy this CTA started land before shared memory is released.
       mbar_wait_quiet(bar_q, 0);
-      for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j) {
-        mbar_wait_quiet(bar_k(j % kStages), (j / kStages) & 1);
-        mbar_wait_quiet(bar_v(j % kStages), (j / kStages) & 1);
-      }
+      drain_ring<kStagesK>(bar_kfull0, issued);
     }
+  } else if (warp == 2) {
+    // ======================= V producer =======================
+    if (lane == 0) tma_prefetch_desc(&p.tm_v);
+    const int issued = produce_ring<kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv, bh,
+                                              lane, abort_flag, p.err);
+    if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
     constexpr uint32_t idesc_s = make_idesc_f16_f32(kBM, kBN, false);  // K-major A and B
     constexpr uint32_t idesc_pv = make_idesc_f16_f32(kBM, kD, true);   // B (= V) MN-major
-    const bool leader = (lane == 0);
+    // The whole warp runs this code with identical values, so the compiler
+    // keeps every MMA operand in uniform registers; one elected lane issues.
+    // (Operands built in lane-0-only code cost ~100 cycles per tcgen05.mma.)
+    // Descriptors advance by constants: +32 B per K step inside a 128B-swizzled
+    // K-major row (encoded +2), +2048 B per 16 keys of MN-major V (encoded +128).
+    const uint32_t tm = __shfl_sync(0xffffffffu, tmem, 0);
+    const uint64_t dq0 = make_sdesc_sw128(s_q[0], 16, 1024);
+    const uint64_t dq1 = make_sdesc_sw128(s_q[1], 16, 1024);
+    const uint64_t dk0 = make_sdesc_sw128(s_k0, 16, 1024);
+    const uint64_t dv0 = make_sdesc_sw128(s_v0, 8192, 1024);
+    constexpr uint64_t kStageEnc = kTileBytes >> 4;  // one stage in descriptor units
     auto issue_s = [&](int i, int st) {
-      if (leader) {
+      const uint64_t a = i ? dq1 : dq0;
+      const uint64_t b = dk0 + static_cast<uint64_t>(st) * kStageEnc;
+      const uint32_t d = tm + col_s(i);
+      if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t a = make_sdesc_sw128(s_q[i] + kk * 32, 16, 1024);
-          const uint64_t b = make_sdesc_sw128(s_k(st) + kk * 32, 16, 1024);
-          umma_f16_ss(tmem + col_s(i), a, b, idesc_s, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kD / 16; ++kk)
+          umma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(bar_s(i));
       }
       __syncwarp();
     };
-    auto issue_pv = [&](int i, int st, int j, bool last) {
-      if (leader) {
+    auto issue_pv = [&](int i, int st, int j) {
+      const uint64_t b = dv0 + static_cast<uint64_t>(st) * kStageEnc;
+      const uint32_t d = tm + col_o(i);
+      const uint32_t a = tm + col_p(i);
+      const uint32_t acc0 = j > 0 ? 1u : 0u;
+      if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t b = make_sdesc_sw128(s_v(st) + kk * 16 * kD * 2, 8192, 1024);
-          umma_f16_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, idesc_pv,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (last) umma_commit(bar_o(i));
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_f16_ts(d, a + kk * 8, b + 128 * kk, idesc_pv, kk > 0 ? 1u : acc0);
+        umma_commit(bar_pv(i));
       }
       __syncwarp();
     };
+    auto commit_to = [&](uint32_t bar) {
+      if (elect_one()) umma_commit(bar);
+      __syncwarp();
+    };
 
-    bool ok = warp_wait(bar_q, 0, abort_flag, p.err);
-    if (ok) ok = warp_wait(bar_k(0), 0, abort_flag, p.err);
-    if (ok) {
+    bool ok = warp_wait_spin(bar_q, 0, abort_flag, p.err);
+    if (ok && nkv > 0) ok = warp_wait_spin(bar_kfull(0), 0, abort_flag, p.err);
+    if (ok && nkv > 0) {
       tc_fence_after();
       if (nkv0 > 0) issue_s(0, 0);
       if (nkv1 > 0) issue_s(1, 0);
+      commit_to(bar_kempty(0));
       for (int j = 0; j < nkv; ++j) {
-        const int st = j % kStages;
-        if (!warp_wait(bar_v(st), (j / kStages) & 1, abort_flag, p.err)) break;
-        if (j < nkv0) {
-          if (!warp_wait(bar_p(0), j & 1, abort_flag, p.err)) break;
-          tc_fence_after();
-          issue_pv(0, st, j, j == nkv0 - 1);
-        }
-        const int st1 = (j + 1) % kStages;
+        // S of the next tile: needs K_{j+1} and the softmax's release of S_j.
         if (j + 1 < nkv) {
-          if (!warp_wait(bar_k(st1), ((j + 1) / kStages) & 1, abort_flag, p.err)) break;
+          const int sk = (j + 1) % kStagesK;
+          if (!warp_wait_spin(bar_kfull(sk), ((j + 1) / kStagesK) & 1, abort_flag, p.err)) break;
+          if (lane == 0) FL_TRACE_EV(10, j);
+          if (j + 1 < nkv0) {
+            if (!warp_wait_spin(bar_sfree(0), j & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            issue_s(0, sk);
+            if (lane == 0) FL_TRACE_EV(12, j);
+          }
+          if (j + 1 < nkv1) {
+            if (!warp_wait_spin(bar_sfree(1), j & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            issue_s(1, sk);
+          }
+          commit_to(bar_kempty(sk));
         }
-        if (j + 1 < nkv0) issue_s(0, st1);
-        if (j < nkv1) {
-          if (!warp_wait(bar_p(1), j & 1, abort_flag, p.err)) break;
+        // P V of this tile.
+        const int sv = j % kStagesV;
+        if (!warp_wait_spin(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
+        if (j < nkv0) {
+          if (!warp_wait_spin(bar_p(0), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          issue_pv(1, st, j, j == nkv1 - 1);
+          if (lane == 0) FL_TRACE_EV(8, j);
+          issue_pv(0, sv, j);
+          if (lane == 0) FL_TRACE_EV(11, j);
         }
-        if (j + 1 < nkv1) issue_s(1, st1);
-        if (leader) umma_commit(bar_empty(st));
-        __syncwarp();
+        if (j < nkv1) {
+          if (!warp_wait_spin(bar_p(1), j & 1, abort_flag, p.err)) break;
+          tc_fence_after();
+          if (lane == 0) FL_TRACE_EV(9, j);
+          issue_pv(1, sv, j);
+          if (lane == 0) FL_TRACE_EV(13, j);
+        }
+        commit_to(bar_vempty(sv));
       }
     }
     // Drain: wait until every MMA this thread issued has completed.
-    if (leader) {
+    if (elect_one()) {
       umma_commit(bar_drain);
       mbar_wait_quiet(bar_drain, 0);
     }
     __syncwarp();
   }
-  // warps 2 and 3 have no role in this design.
+  // warp 3 has no role in this design.
   } else {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n");
   {
@@ -298,9 +398,15 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
 
     for (int j = 0; j < my_nkv; ++j) {
       if (!warp_wait(bar_s(i), j & 1, abort_flag, p.err)) { ok = false; break; }
+      if (t == 0) FL_TRACE_EV(0 + 4 * i, j);
       tc_fence_after();
       uint32_t sr[128];
       tmem_ld128_wait(tS, sr);
+      // S_i is in registers: let the tensor core overwrite it with S_{i,j+1}.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree(i));
+      if (t == 0) FL_TRACE_EV(1 + 4 * i, j);
       float s[128];
 #pragma unroll
       for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
@@ -322,9 +428,43 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
       }
-      float mx = s[0];
+      // Row maximum, kept separately over the columns exponentiated on the
+      // FMA pipe (mxp) and on the MUFU (mxm): 3-input max chains, several
+      // independent per class (no 127-long dependency chain).
+      float mxp, mxm;
+      {
+        constexpr int kNP = 12 * 4, kNM = 128 - kNP;  // per row: 48 / 80 columns
+        float vp[kNP], vm[kNM];
+        int np = 0, nm = 0;
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        for (int c = 0; c < 128; c += 2) {
+          const int e = (c >> 1) & 15;
+          if ((kPolyPairs >> (e & 7)) & 1) {
+            vp[np++] = s[c];
+            vp[np++] = s[c + 1];
+          } else {
+            vm[nm++] = s[c];
+            vm[nm++] = s[c + 1];
+          }
+        }
+        float ap[4], am[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          // vp: 12 per chain, vm: 20 per chain
+          float a = fmax3(vp[12 * g], vp[12 * g + 1], vp[12 * g + 2]);
+#pragma unroll
+          for (int e = 3; e < 12; e += 2) a = fmax3(a, vp[12 * g + e], vp[12 * g + e + 1]);
+          ap[g] = fmaxf(a, vp[12 * g + 11]);
+          float b = fmax3(vm[20 * g], vm[20 * g + 1], vm[20 * g + 2]);
+#pragma unroll
+          for (int e = 3; e < 19; e += 2) b = fmax3(b, vm[20 * g + e], vm[20 * g + e + 1]);
+          am[g] = fmaxf(b, vm[20 * g + 19]);
+        }
+        mxp = fmax3(fmaxf(ap[0], ap[1]), ap[2], ap[3]);
+        mxm = fmax3(fmaxf(am[0], am[1]), am[2], am[3]);
+      }
+      const float mx = fmaxf(mxp, mxm);
+      if (t == 0) FL_TRACE_EV(2 + 4 * i, j);
       const float m_tile = mx * scl;
       const float m_new = fmaxf(m_ref, m_tile);
       const bool need = m_new > m_ref + kRescaleThreshold;
@@ -334,40 +474,70 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         m_ref = m_new;
       }
       l *= alpha;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // PV of the previous tile has completed: the commit behind bar_s(i)
-        // tracks every MMA issued before this tile's S.
-        uint32_t o[32];
+      if (j > 0) {
+        // P V of the previous tile must be done before its P columns are
+        // rewritten and before O is rescaled.
+        if (!warp_wait(bar_pv(i), (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+          uint32_t o[32];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          tmem_ld32_wait(tO + h * 32, o);
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld32_wait(tO + h * 32, o);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(tO + h * 32, o);
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(tO + h * 32, o);
+          }
         }
       }
       const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
+      // p = 2^(s*scale - m_use): packed fp32x2 FMA for the argument, MUFU ex2,
+      // fp16x2 pack for the PV operand; l sums the unrounded p in four
+      // independent packed partial sums.
+      const float2 scl2 = make_float2(scl, scl);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+      float2 lsum[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int c = q * 32 + 2 * e;
-          const float p0 = ex2_approx(fmaf(s[c], scl, -m_use));
-          const float p1 = ex2_approx(fmaf(s[c + 1], scl, -m_use));
-          l += p0 + p1;
-          pk[e] = pack_f16x2(p0, p1);
+          const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), scl2, nm2);
+          // Column pairs in kPolyPairs take the FMA-pipe exp2; the rest the
+          // MUFU. Splitting the work keeps both pipes busy.
+          const float2 pp = ((kPolyPairs >> (e & 7)) & 1)
+                                ? exp2_poly2(x)
+                                : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          lsum[e & 3] = __fadd2_rn(lsum[e & 3], pp);
+          pk[e] = pack_f16x2(pp.x, pp.y);
         }
         tmem_st16(tP + q * 16, pk);
+      }
+      {
+        const float2 a = __fadd2_rn(lsum[0], lsum[1]);
+        const float2 b = __fadd2_rn(lsum[2], lsum[3]);
+        l += (a.x + a.y) + (b.x + b.y);
+        // The tile's largest p enters O through its fp16 rounding; let l see
+        // the same value so a row dominated by one key reproduces that key's
+        // V row exactly (the reference gets this for free since its running
+        // maximum is always exact, csrc/kernel_flash2.cu:250-264).
+        // Recompute that p with the method its column used.
+        const float xm = fmaf(mx, scl, -m_use);
+        const float pm = (mxp >= mxm) ? exp2_poly2(make_float2(xm, xm)).x : ex2_approx(xm);
+        l += __half2float(__float2half_rn(pm)) - pm;
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p(i));
+      if (t == 0) FL_TRACE_EV(3 + 4 * i, j);
+      if (t == 96) FL_TRACE_EV(14 + i, j);
     }
 
     // ---- epilogue ----
-    if (active && my_nkv > 0 && ok) ok = warp_wait(bar_o(i), 0, abort_flag, p.err);
+    if (active && my_nkv > 0 && ok) ok = warp_wait(bar_pv(i), (my_nkv - 1) & 1, abort_flag, p.err);
     const bool do_out = active && my_nkv > 0 && ok;
     uint32_t o[64];
     if (do_out) {

@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_runtime.h>
 
 namespace fl {
 
@@ -77,6 +78,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > FL_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      if (err) atomicOr(err, kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// Non-suspending probe of phase `parity` (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that never suspends the thread (test_wait spin). Used by the
+// warp that issues tcgen05.mma: while that warp sits suspended in try_wait,
+// MMAs it issued just before are not started, which stalls the pipeline.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > FL_WAIT_LIMIT_NS) {
       *abort_flag = 1;
@@ -194,6 +226,17 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// True in exactly one lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "elect.sync _|P1, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -306,6 +349,36 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for a pair of floats on the FMA pipe (no MUFU). x = j + f with
+// j = floor(x) and f in [0, 1): 2^f comes from a cubic fitted for minimax
+// relative error (1.03e-4, with p(0) = 1 and p(1) = 2 exactly; see
+// csrc/fit_exp2_poly.py) and j is added to the exponent field as an integer.
+// floor(x) comes from adding 1.5 * 2^23 with round-toward-minus-infinity: the
+// sum's low mantissa bits then hold floor(x), so (bits(t) << 23) is j placed
+// in the exponent field (mod 2^32). Inputs are clamped to >= -127; 2^-127
+// and below vanish in the fp16 rounding of P anyway. Valid for x <= 127.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC1 = 0.6954243f, kC2 = 0.22630768f, kC3 = 0.07826797f;
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -127.0f);
+  x.y = fmaxf(x.y, -127.0f);
+  const float2 t = __fadd2_rd(x, make_float2(kMagic, kMagic));           // kMagic + floor(x)
+  const float2 j = __fadd2_rn(t, make_float2(-kMagic, -kMagic));         // floor(x), exact
+  const float2 f = __fadd2_rn(x, make_float2(-j.x, -j.y));               // [0, 1), exact
+  float2 p = __ffma2_rn(f, make_float2(kC3, kC3), make_float2(kC2, kC2));
+  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
+  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// Three-input maximum (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Pack two floats as f16x2 with round-to-nearest-even; `lo` lands in the low
