@@ -9,26 +9,27 @@ Drop-in for the ``flash_attn_wmma`` extension of thebigblender/FlashLite::
 Multi-GPU helpers live in :mod:`flashlite_b200.parallel_attn` (head sharding
 and ring attention over NCCL). The native code is the in-tree
 ``libflashlite_b200.so`` (C ABI, ``include/flashlite_b200.h``) and the torch
-binding ``_C``; importing this package fails loudly if they are missing.
+binding ``_C``, built by ``python -m flashlite_b200.build``. Importing
+``flash_attn_wmma`` fails loudly if they are missing; there is no fallback.
 """
 from __future__ import annotations
 
 from pathlib import Path
 
-import torch  # noqa: F401  (loads libtorch/libc10 for the binding)
-
 _PKG = Path(__file__).resolve().parent
 LIBRARY_PATH = _PKG / "libflashlite_b200.so"
 
-try:
-    from . import _C  # noqa: E402
-except ImportError as exc:  # pragma: no cover - exercised only on broken installs
-    raise ImportError(
-        "flashlite_b200 native extension is not built; run `python -m flashlite_b200.build` "
-        f"(or __graft_entry__.build()): {exc}"
-    ) from exc
+__version__ = "0.1.0"
 
-from . import flash_attn_wmma  # noqa: E402
+
+def __getattr__(name):
+    # Lazy so that the build script (a submodule) can run before the native
+    # extension exists; any use of the drop-in module imports it for real.
+    if name == "flash_attn_wmma":
+        from . import flash_attn_wmma
+
+        return flash_attn_wmma
+    raise AttributeError(name)
+
 
 __all__ = ["flash_attn_wmma", "LIBRARY_PATH"]
-__version__ = "0.1.0"

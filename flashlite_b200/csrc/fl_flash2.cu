@@ -71,8 +71,27 @@ constexpr float kRescaleThreshold = 8.0f;
 #define FL_POLY_PAIRS 0x92
 #endif
 constexpr unsigned kPolyPairs = FL_POLY_PAIRS;
-static_assert(__builtin_popcount(kPolyPairs & 0xff) == 3,
-              "the split row-max below assumes 3 of 8 column pairs on the FMA pipe");
+constexpr int kPolyCols = 16 * __builtin_popcount(kPolyPairs & 0xffu);  // per 128-col row
+static_assert(kPolyCols >= 8 && kPolyCols <= 120, "both exp methods must get columns");
+
+// Maximum of N values in four independent chains of 3-input max.
+template <int N>
+__device__ __forceinline__ float max_chains4(const float* v) {
+  static_assert(N % 4 == 0 && N >= 8, "N must be a multiple of 4, at least 8");
+  constexpr int L = N / 4;
+  float part[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float* w = v + g * L;
+    float a = fmaxf(w[0], w[1]);
+    int e = 2;
+#pragma unroll
+    for (; e + 1 < L; e += 2) a = fmax3(a, w[e], w[e + 1]);
+    if (e < L) a = fmaxf(a, w[e]);
+    part[g] = a;
+  }
+  return fmax3(fmaxf(part[0], part[1]), part[2], part[3]);
+}
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
 constexpr int kSmemQ = 0;                                  // 2 tiles
@@ -120,10 +139,10 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
-// Variant for the MMA-issuing warp: spins without suspending.
-__device__ __forceinline__ bool warp_wait_spin(uint32_t bar, uint32_t parity,
-                                               volatile int* abort_flag, unsigned int* err) {
-  const bool ok = mbar_wait_spin(bar, parity, abort_flag, err);
+// Variant for the MMA-issuing warp (see mbar_wait_issuer).
+__device__ __forceinline__ bool warp_wait_issuer(uint32_t bar, uint32_t parity,
+                                                 volatile int* abort_flag, unsigned int* err) {
+  const bool ok = mbar_wait_issuer(bar, parity, abort_flag, err);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -322,8 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       __syncwarp();
     };
 
-    bool ok = warp_wait_spin(bar_q, 0, abort_flag, p.err);
-    if (ok && nkv > 0) ok = warp_wait_spin(bar_kfull(0), 0, abort_flag, p.err);
+    bool ok = warp_wait_issuer(bar_q, 0, abort_flag, p.err);
+    if (ok && nkv > 0) ok = warp_wait_issuer(bar_kfull(0), 0, abort_flag, p.err);
     if (ok && nkv > 0) {
       tc_fence_after();
       if (nkv0 > 0) issue_s(0, 0);
@@ -333,16 +352,16 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         // S of the next tile: needs K_{j+1} and the softmax's release of S_j.
         if (j + 1 < nkv) {
           const int sk = (j + 1) % kStagesK;
-          if (!warp_wait_spin(bar_kfull(sk), ((j + 1) / kStagesK) & 1, abort_flag, p.err)) break;
+          if (!warp_wait_issuer(bar_kfull(sk), ((j + 1) / kStagesK) & 1, abort_flag, p.err)) break;
           if (lane == 0) FL_TRACE_EV(10, j);
           if (j + 1 < nkv0) {
-            if (!warp_wait_spin(bar_sfree(0), j & 1, abort_flag, p.err)) break;
+            if (!warp_wait_issuer(bar_sfree(0), j & 1, abort_flag, p.err)) break;
             tc_fence_after();
             issue_s(0, sk);
             if (lane == 0) FL_TRACE_EV(12, j);
           }
           if (j + 1 < nkv1) {
-            if (!warp_wait_spin(bar_sfree(1), j & 1, abort_flag, p.err)) break;
+            if (!warp_wait_issuer(bar_sfree(1), j & 1, abort_flag, p.err)) break;
             tc_fence_after();
             issue_s(1, sk);
           }
@@ -350,16 +369,16 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         }
         // P V of this tile.
         const int sv = j % kStagesV;
-        if (!warp_wait_spin(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
+        if (!warp_wait_issuer(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
         if (j < nkv0) {
-          if (!warp_wait_spin(bar_p(0), j & 1, abort_flag, p.err)) break;
+          if (!warp_wait_issuer(bar_p(0), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
           if (lane == 0) FL_TRACE_EV(8, j);
           issue_pv(0, sv, j);
           if (lane == 0) FL_TRACE_EV(11, j);
         }
         if (j < nkv1) {
-          if (!warp_wait_spin(bar_p(1), j & 1, abort_flag, p.err)) break;
+          if (!warp_wait_issuer(bar_p(1), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
           if (lane == 0) FL_TRACE_EV(9, j);
           issue_pv(1, sv, j);
@@ -433,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       // independent per class (no 127-long dependency chain).
       float mxp, mxm;
       {
-        constexpr int kNP = 12 * 4, kNM = 128 - kNP;  // per row: 48 / 80 columns
+        constexpr int kNP = kPolyCols, kNM = 128 - kNP;  // per row
         float vp[kNP], vm[kNM];
         int np = 0, nm = 0;
 #pragma unroll
@@ -447,21 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
             vm[nm++] = s[c + 1];
           }
         }
-        float ap[4], am[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          // vp: 12 per chain, vm: 20 per chain
-          float a = fmax3(vp[12 * g], vp[12 * g + 1], vp[12 * g + 2]);
-#pragma unroll
-          for (int e = 3; e < 12; e += 2) a = fmax3(a, vp[12 * g + e], vp[12 * g + e + 1]);
-          ap[g] = fmaxf(a, vp[12 * g + 11]);
-          float b = fmax3(vm[20 * g], vm[20 * g + 1], vm[20 * g + 2]);
-#pragma unroll
-          for (int e = 3; e < 19; e += 2) b = fmax3(b, vm[20 * g + e], vm[20 * g + e + 1]);
-          am[g] = fmaxf(b, vm[20 * g + 19]);
-        }
-        mxp = fmax3(fmaxf(ap[0], ap[1]), ap[2], ap[3]);
-        mxm = fmax3(fmaxf(am[0], am[1]), am[2], am[3]);
+        mxp = max_chains4<kNP>(vp);
+        mxm = max_chains4<kNM>(vm);
       }
       const float mx = fmaxf(mxp, mxm);
       if (t == 0) FL_TRACE_EV(2 + 4 * i, j);

@@ -68,47 +68,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`. Returns false (after recording
-// kDevErrWaitTimeout in *err and raising the CTA abort flag) if the phase does
-// not complete within FL_WAIT_LIMIT_NS, or if another role of this CTA has
-// already aborted. Never spins forever.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > FL_WAIT_LIMIT_NS) {
-      *abort_flag = 1;
-      if (err) atomicOr(err, kDevErrWaitTimeout);
-      return false;
-    }
-  }
-}
-
-// Non-suspending probe of phase `parity` (mbarrier.test_wait).
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+// try_wait with an explicit suspend-time hint (nanoseconds): the thread
+// sleeps until the phase completes or the hint expires.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(ns)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait that never suspends the thread (test_wait spin). Used by the
-// warp that issues tcgen05.mma: while that warp sits suspended in try_wait,
-// MMAs it issued just before are not started, which stalls the pipeline.
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                               unsigned int* err) {
-  if (mbar_test_wait(bar, parity)) return true;
+// Bounded wait for phase `parity` of `bar`. Returns false (after recording
+// kDevErrWaitTimeout in *err and raising the CTA abort flag) if the phase does
+// not complete within FL_WAIT_LIMIT_NS, or if another role of this CTA has
+// already aborted. Never waits forever. Waiting threads sleep in try_wait
+// (suspend hint `hint_ns`) and look at the clock and the abort flag only
+// every 16 probes, so a waiting warp takes almost no issue slots from the
+// warps that are working.
+__device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity,
+                                                 volatile int* abort_flag, unsigned int* err,
+                                                 uint32_t hint_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_test_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k)
+      if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > FL_WAIT_LIMIT_NS) {
       *abort_flag = 1;
@@ -116,6 +105,27 @@ __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, vo
       return false;
     }
   }
+}
+
+#ifndef FL_WAIT_HINT_NS
+#define FL_WAIT_HINT_NS 20000
+#endif
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int* err) {
+  return mbar_wait_hinted(bar, parity, abort_flag, err, FL_WAIT_HINT_NS);
+}
+
+// Bounded wait for the warp that issues tcgen05.mma. Measured on B200: while
+// that warp sits suspended in try_wait for long, MMAs it issued just before
+// are not started until it resumes, stalling the pipeline by microseconds; a
+// busy test_wait spin avoids that but steals issue slots from the softmax
+// warps on the same SM sub-partition. A short suspend hint does neither.
+#ifndef FL_ISSUER_HINT_NS
+#define FL_ISSUER_HINT_NS 40
+#endif
+__device__ __forceinline__ bool mbar_wait_issuer(uint32_t bar, uint32_t parity,
+                                                 volatile int* abort_flag, unsigned int* err) {
+  return mbar_wait_hinted(bar, parity, abort_flag, err, FL_ISSUER_HINT_NS);
 }
 
 // Drain-time wait: bounded, reports nothing (the caller already failed).

@@ -12,7 +12,8 @@ thebigblender/FlashLite ``csrc/flash_attn.cpp:4-29``:
 
 Invalid inputs raise ``RuntimeError`` with the reference's messages. The
 functions are the C++ binding's own (``flashlite_b200._C``); there is no
-Python or CPU fallback.
+Python or CPU fallback: importing this module without the built native code
+raises ImportError.
 
 Extra entry points (no reference counterpart) used by ring attention:
 ``forward_block`` and ``ring_finalize``; ``device_error`` reads the error
@@ -20,6 +21,14 @@ bits kernels raise when a bounded wait gives up.
 """
 from __future__ import annotations
 
-from ._C import device_error, forward_block, forward_flash2, forward_naive, ring_finalize
+import torch  # noqa: F401  (loads libtorch/libc10 for the binding)
+
+try:
+    from ._C import device_error, forward_block, forward_flash2, forward_naive, ring_finalize
+except ImportError as exc:  # pragma: no cover - exercised only on unbuilt trees
+    raise ImportError(
+        "flashlite_b200 native extension is not built; run `python -m flashlite_b200.build` "
+        f"(or __graft_entry__.build()): {exc}"
+    ) from exc
 
 __all__ = ["forward_flash2", "forward_naive", "forward_block", "ring_finalize", "device_error"]
