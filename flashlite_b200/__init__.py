@@ -26,9 +26,9 @@ def __getattr__(name):
     # Lazy so that the build script (a submodule) can run before the native
     # extension exists; any use of the drop-in module imports it for real.
     if name == "flash_attn_wmma":
-        from . import flash_attn_wmma
+        import importlib
 
-        return flash_attn_wmma
+        return importlib.import_module(__name__ + ".flash_attn_wmma")
     raise AttributeError(name)
 
 
