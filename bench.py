@@ -48,6 +48,7 @@ WORKLOADS = {
     "cfg3": (2, 8, 4096, False, "BASELINE config 3: B2 H8 N4096 D64 non-causal (headline)"),
     "cfg3c": (2, 8, 4096, True, "BASELINE config 3: B2 H8 N4096 D64 causal"),
     "cfg4": (16, 32, 8192, True, "BASELINE config 4: B16 H32 N8192 D64 causal, 512 slices split over ranks"),
+    "cfg5": (1, 8, 131072, True, "BASELINE config 5: B1 H8 N131072 D64 causal, sequence sharded, NCCL ring"),
 }
 
 
@@ -329,57 +330,171 @@ def run_ours(args):
 
 
 # ----------------------------------------------------------------------------
+# config 5: sequence-sharded ring attention (strong scaling over ranks)
+# ----------------------------------------------------------------------------
+def run_ring(args):
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    init_dist(world, "nccl")
+    from flashlite_b200 import flash_attn_wmma as fa
+    from flashlite_b200.parallel_attn import RingAttention
+
+    B, H, N, causal, desc = WORKLOADS["cfg5"]
+    D, sm_scale = 64, 0.125
+    assert N % world == 0
+    nb = N // world
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    q, k, v = ((torch.randn(B, H, nb, D, generator=g, device=device) * 0.5).to(torch.float16)
+               for _ in range(3))
+    out = torch.empty_like(q)
+    o_acc = torch.empty(B, H, nb, D, dtype=torch.float32, device=device)
+    lse = torch.empty(B, H, nb, dtype=torch.float32, device=device)
+    ring = RingAttention() if world > 1 else None
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+
+    def step():
+        if ring is None:
+            fa.forward_flash2(q, k, v, sm_scale, causal, out=out)
+        else:
+            ring.forward(q, k, v, sm_scale, causal, out=out, o_acc=o_acc, lse=lse)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(device.index) as clk:
+        for a, b in evs:
+            flush.zero_()  # untimed: evicts this rank's blocks from L2
+            a.record()
+            step()
+            b.record()
+        torch.cuda.synchronize(device)
+    barrier(world, device)
+    ms_local = sum(a.elapsed_time(b) for a, b in evs)
+    ms = max_over_ranks(ms_local, world, device)
+    ms_step = ms / args.steps
+    total_flops = flops(B, H, N, D, causal)
+    value = total_flops / (ms_step * 1e-3) / 1e12
+
+    # end to end: this rank's blocks from pinned host memory, output back
+    qp, kp, vp = (t.cpu().pin_memory() for t in (q, k, v))
+    op = torch.empty_like(qp).pin_memory()
+
+    def e2e_step():
+        q.copy_(qp, non_blocking=True)
+        k.copy_(kp, non_blocking=True)
+        v.copy_(vp, non_blocking=True)
+        step()
+        op.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    e_steps = max(2, min(args.steps, 5))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e_ms = max_over_ranks(e0.elapsed_time(e1) / e_steps, world, device)
+    err = fa.device_error()
+    peak_burst, peak_sust, _, peak_kind = measured_peaks()
+    per_gpu = value / world
+    if rank == 0:
+        line = {
+            "metric": "FA2 fwd TFLOP/s per B200 (fp16, D=64)", "value": round(value, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+            "data": "synthetic: seeded i.i.d. N(0,1)*0.5 fp16 Q/K/V generated per rank on device",
+            "config": {"workload": desc, "B": B, "H": H, "N": N, "D": D, "causal": True,
+                       "rows_per_rank": nb,
+                       "parallelism": f"ring x{world} (NCCL send/recv)" if world > 1 else "single GPU",
+                       "l2": "256 MiB buffer written between timed steps (untimed)"},
+            "pct_of_peak": round(100 * per_gpu / peak_burst, 2),
+            "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak_burst,
+                         "unit": "TFLOP/s", "frac": round(per_gpu / peak_burst, 4),
+                         "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
+                         "traffic": None,
+                         "note": "per GPU; causal contiguous blocks cap the ideal ring speedup at P^2/(2P-1)"},
+            "e2e": {"value": round(total_flops / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
+                    "ms_per_step": round(e_ms, 3)},
+            "gpu_launches": args.steps * (world if world > 1 else 1),
+            "clocks": clk.summary(),
+            "device_error": int(err),
+        }
+        print(json.dumps(line), flush=True)
+    if ring is not None:
+        del ring
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
 # CPU baseline (oracle port, torch fp32 on host cores)
 # ----------------------------------------------------------------------------
-def cpu_sample(workload):
+def cpu_step(workload):
+    """One bounded CPU sample of the workload: (callable, FLOPs, description).
+
+    torch fp32 matmul-softmax-matmul (the oracle port). Config 5 is sampled
+    by query rows (its full score matrix would need 64 GB): the last 256 rows
+    of one head, each attending to its whole causal prefix."""
+    from oracle.attention_oracle import attention_fp32, attention_rows_fp32, make_qkv
+
     B, H, N, causal, _ = WORKLOADS[workload]
+    if workload == "cfg5":
+        R = 256
+        q, k, v = make_qkv(1, 1, N, 64, seed=0, scale=0.5)
+        q3, k3, v3 = (t.view(1, N, 64) for t in (q, k, v))
+        rows = torch.arange(N - R, N)
+        f = float(sum(4 * (int(r) + 1) * 64 for r in rows))
+        return (lambda: attention_rows_fp32(q3, k3, v3, rows, 0.125, True), f,
+                f"last {R} query rows of 1 of the {H} heads (N={N}, causal), row-sampled")
     n_slices = {"cfg2": 16, "cfg2c": 16, "cfg3": 4, "cfg3c": 4, "cfg4": 1}[workload]
-    return n_slices, N, causal
+    q, k, v = make_qkv(1, n_slices, N, 64, seed=0)
+    return (lambda: attention_fp32(q, k, v, 0.125, causal), flops(1, n_slices, N, 64, causal),
+            f"{n_slices} of the workload's (b,h) slices (N={N}, causal={causal})")
 
 
 def cpu_baseline(workload, reps=3):
-    from oracle.attention_oracle import attention_fp32, make_qkv
-
-    n_slices, N, causal = cpu_sample(workload)
-    q, k, v = make_qkv(1, n_slices, N, 64, seed=0)
+    fn, f, desc = cpu_step(workload)
     ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        attention_fp32(q, k, v, 0.125, causal)
+        fn()
         ts.append(time.perf_counter() - t0)
     t = sorted(ts)[len(ts) // 2]
-    f = flops(1, n_slices, N, 64, causal)
     return {"value": round(f / t / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{n_slices} of the workload's (b,h) slices (N={N}, causal={causal}), "
-                      f"torch fp32 matmul-softmax-matmul, median of {reps}: {t * 1e3:.1f} ms"}
+            "sample": f"{desc}; torch fp32 matmul-softmax-matmul, median of {reps}: {t * 1e3:.1f} ms"}
 
 
 def run_reference(args):
     world, rank, local = dist_env()
     if rank != 0:
         return  # the reference arm runs on rank 0 only
-    from oracle.attention_oracle import attention_fp32, make_qkv
-
-    n_slices, N, causal = cpu_sample(args.workload)
-    q, k, v = make_qkv(1, n_slices, N, 64, seed=0)
+    fn, f, desc = cpu_step(args.workload)
     for _ in range(args.warmup):
-        attention_fp32(q, k, v, 0.125, causal)
+        fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        attention_fp32(q, k, v, 0.125, causal)
+        fn()
     dt = (time.perf_counter() - t0) / args.steps
-    f = flops(1, n_slices, N, 64, causal)
     value = f / dt / 1e12
-    sample = (f"{n_slices} of the workload's (b,h) slices per step (N={N}, causal={causal}); "
-              "torch fp32 matmul-softmax-matmul on host cores")
+    B, H, N, causal, _ = WORKLOADS[args.workload]
+    sample = f"{desc} per step; torch fp32 matmul-softmax-matmul on host cores"
     line = {
         "metric": "FA2 fwd TFLOP/s per B200 (fp16, D=64)", "impl": "reference",
         "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic: seeded i.i.d. N(0,1) fp16 Q/K/V generated on host",
-        "config": {"workload": WORKLOADS[args.workload][4], "sample_slices": n_slices, "N": N,
+        "config": {"workload": WORKLOADS[args.workload][4], "sample": desc, "N": N,
                    "D": 64, "causal": causal},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s",
                          "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
@@ -462,6 +577,8 @@ def main():
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg5":
+        run_ring(args)
     else:
         run_ours(args)
 
