@@ -61,6 +61,8 @@ unsigned int* device_error_word() {
   return (dev >= 0 && dev < kMaxDevices) ? g_err_ptr[dev] : nullptr;
 }
 
+bool prepare_current_device() { return init_device(current_device()); }
+
 int sm_count() {
   const int dev = current_device();
   return (dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) ? g_sm_count[dev] : 148;

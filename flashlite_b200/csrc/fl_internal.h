@@ -17,6 +17,10 @@ unsigned int* device_error_word();
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Caches the current device's attributes and error-word address (what the
+// C-ABI entry points do before their first launch); false on failure.
+bool prepare_current_device();
+
 // Launchers. All sizes validated by the caller; return 0 or a cudaError_t.
 cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
                           float* lse, int64_t BH, int64_t Nq, int64_t Nk, int64_t q_offset,

@@ -72,6 +72,30 @@ int fl_flash2_fwd_block(const void* q, const void* k, const void* v, float* o_ac
  */
 int fl_ring_finalize(const float* o_acc, void* o, int64_t n_elems, void* stream);
 
+/*
+ * Allocation-free block step. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory when they call this library:
+ * a host runtime that owns all device memory and hands out nothing after
+ * start-up, or a latency-critical path where an allocation could stall or
+ * fail. Same computation as fl_flash2_fwd_block, but the running state
+ * (normalised fp32 output and log-sum-exp of B*H*Nq rows) lives in a fixed
+ * 16.25 MiB array inside the library instead of caller buffers; nothing is
+ * allocated. `first` != 0 starts a new accumulation (it overwrites the
+ * state); `last` != 0 also writes the fp16 result to o [BH, Nq, 64] (o may
+ * be NULL otherwise). Limits: D == 64 and BH*Nq <= 65536 rows, else
+ * FL_ERR_UNSUPPORTED. Every GPU that loads the library holds the array until
+ * the process exits. All calls on a device share that one array and it keeps
+ * the last call's contents: a first..last sequence must not be interleaved
+ * with another one, and calls that overlap on the GPU (other streams or
+ * threads) race. The first call on each device looks up the array's device
+ * address; make that first call before any stream capture begins.
+ */
+int fl_flash2_fwd_block_noalloc(const void* q, const void* k, const void* v, void* o,
+                                int64_t BH, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
+                                int64_t kv_offset, float sm_scale, int is_causal, int first,
+                                int last, void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* fl_status_str(int status);
 
