@@ -461,7 +461,16 @@ def cpu_step(workload):
             f"{n_slices} of the workload's (b,h) slices (N={N}, causal={causal})")
 
 
+def use_all_host_cores() -> int:
+    """torchrun sets OMP_NUM_THREADS=1 for every rank; the CPU arm runs on rank
+    0 alone and may use every core this process is allowed on."""
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_baseline(workload, reps=3):
+    use_all_host_cores()
     fn, f, desc = cpu_step(workload)
     ts = []
     for _ in range(reps):
@@ -478,6 +487,7 @@ def run_reference(args):
     world, rank, local = dist_env()
     if rank != 0:
         return  # the reference arm runs on rank 0 only
+    use_all_host_cores()
     fn, f, desc = cpu_step(args.workload)
     for _ in range(args.warmup):
         fn()
