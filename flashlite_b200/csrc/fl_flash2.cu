@@ -21,6 +21,10 @@
 //    them (barrier s_free), so S_{j+1} = Q K_{j+1}^T runs on the tensor core
 //    while tile j is still being exponentiated; the only wait left on the
 //    softmax path is for P V of the previous tile (its P columns are reused).
+//    The two warpgroups run half a KV tile apart: every SM sub-partition
+//    holds one warp of each, and while one waits on a barrier or a TMEM round
+//    trip (each costs a few hundred cycles while the other warp keeps the
+//    MUFU queue full) the other computes.
 //  * O is rescaled only when a row maximum grows by more than 2^8 (O and l
 //    always share one reference maximum, so the result is unchanged up to
 //    rounding), which removes almost every TMEM round trip of O.
@@ -66,9 +70,10 @@ __host__ __device__ constexpr uint32_t col_p(int i) { return i ? 448u : 384u; } 
 constexpr float kRescaleThreshold = 8.0f;
 
 // Bit e set: column pair e (mod 8) of every 16-column group is exponentiated
-// on the FMA pipe (exp2_poly2) instead of the MUFU (3 of 8 pairs).
+// on the FMA pipe (exp2_poly2) instead of the MUFU (2 of 8 pairs; with the
+// two tiles staggered, 1/8 and 2/8 measure the same and 3/8 or more is slower).
 #ifndef FL_POLY_PAIRS
-#define FL_POLY_PAIRS 0x92
+#define FL_POLY_PAIRS 0x11
 #endif
 constexpr unsigned kPolyPairs = FL_POLY_PAIRS;
 constexpr int kPolyCols = 16 * __builtin_popcount(kPolyPairs & 0xffu);  // per 128-col row
@@ -98,8 +103,8 @@ constexpr int kSmemQ = 0;                                  // 2 tiles
 constexpr int kSmemK = kSmemQ + 2 * kTileBytes;            // kStagesK tiles
 constexpr int kSmemV = kSmemK + kStagesK * kTileBytes;     // kStagesV tiles
 constexpr int kSmemBar = kSmemV + kStagesV * kTileBytes;   // mbarriers
-// q | k full/empty | v full/empty | s_full, s_free, p_full, pv_done (x2) | drain
-constexpr int kNumBars = 1 + 2 * kStagesK + 2 * kStagesV + 4 * 2 + 1;
+// q | k full/empty | v full/empty | s_full, s_free, p_full, pv_done (x2) | drain | stagger
+constexpr int kNumBars = 1 + 2 * kStagesK + 2 * kStagesV + 4 * 2 + 2;
 constexpr int kSmemMisc = kSmemBar + kNumBars * 8;         // tmem base, abort flag
 constexpr int kSmemBytes = kSmemMisc + 16;
 constexpr int kSmemAlloc = kSmemBytes + 1024;              // alignment slack
@@ -215,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   auto bar_p = [&](int i) { return bar_x0 + 8u * (4 + i); };       // P_i written
   auto bar_pv = [&](int i) { return bar_x0 + 8u * (6 + i); };      // P_i V done (O_i updated)
   const uint32_t bar_drain = bar_x0 + 8u * 8;
+  const uint32_t bar_stagger = bar_x0 + 8u * 9;  // tile 0 half-way through its first tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
 
@@ -255,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       mbar_init(bar_pv(i), 1);
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_stagger, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -348,43 +355,53 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (nkv0 > 0) issue_s(0, 0);
       if (nkv1 > 0) issue_s(1, 0);
       commit_to(bar_kempty(0));
-      for (int j = 0; j < nkv; ++j) {
-        // S of the next tile: needs K_{j+1} and the softmax's release of S_j.
-        if (j + 1 < nkv) {
-          const int sk = (j + 1) % kStagesK;
+      // Issue order per iteration j, matching the staggered softmax tiles
+      // (tile 1 runs about half a KV step behind tile 0): S_0(j+1),
+      // P_1(j-1) V, S_1(j+1), P_0(j) V. Each MMA waits only for its own
+      // inputs, so neither tile's softmax waits behind the other's.
+      for (int j = 0; j <= nkv; ++j) {
+        const bool s_next = j + 1 < nkv;
+        const int sk = (j + 1) % kStagesK;
+        if (s_next) {
           if (!warp_wait_issuer(bar_kfull(sk), ((j + 1) / kStagesK) & 1, abort_flag, p.err)) break;
           if (lane == 0) FL_TRACE_EV(10, j);
-          if (j + 1 < nkv0) {
-            if (!warp_wait_issuer(bar_sfree(0), j & 1, abort_flag, p.err)) break;
-            tc_fence_after();
-            issue_s(0, sk);
-            if (lane == 0) FL_TRACE_EV(12, j);
-          }
-          if (j + 1 < nkv1) {
-            if (!warp_wait_issuer(bar_sfree(1), j & 1, abort_flag, p.err)) break;
-            tc_fence_after();
-            issue_s(1, sk);
-          }
-          commit_to(bar_kempty(sk));
         }
-        // P V of this tile.
-        const int sv = j % kStagesV;
-        if (!warp_wait_issuer(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
-        if (j < nkv0) {
-          if (!warp_wait_issuer(bar_p(0), j & 1, abort_flag, p.err)) break;
+        if (j + 1 < nkv0) {
+          if (!warp_wait_issuer(bar_sfree(0), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          if (lane == 0) FL_TRACE_EV(8, j);
-          issue_pv(0, sv, j);
-          if (lane == 0) FL_TRACE_EV(11, j);
+          issue_s(0, sk);
+          if (lane == 0) FL_TRACE_EV(12, j);
         }
-        if (j < nkv1) {
-          if (!warp_wait_issuer(bar_p(1), j & 1, abort_flag, p.err)) break;
+        if (j >= 1) {
+          // P_1 V of the previous KV tile, then that V stage is free.
+          const int sv = (j - 1) % kStagesV;
+          if (j - 1 < nkv1) {
+            if (!warp_wait_issuer(bar_p(1), (j - 1) & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            if (lane == 0) FL_TRACE_EV(9, j - 1);
+            issue_pv(1, sv, j - 1);
+            if (lane == 0) FL_TRACE_EV(13, j - 1);
+          }
+          commit_to(bar_vempty(sv));
+        }
+        if (j + 1 < nkv1) {
+          if (!warp_wait_issuer(bar_sfree(1), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          if (lane == 0) FL_TRACE_EV(9, j);
-          issue_pv(1, sv, j);
-          if (lane == 0) FL_TRACE_EV(13, j);
+          issue_s(1, sk);
         }
-        commit_to(bar_vempty(sv));
+        if (s_next) commit_to(bar_kempty(sk));
+        if (j < nkv) {
+          // V_j must be resident for P_0 V (and later P_1 V).
+          const int sv = j % kStagesV;
+          if (!warp_wait_issuer(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
+          if (j < nkv0) {
+            if (!warp_wait_issuer(bar_p(0), j & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            if (lane == 0) FL_TRACE_EV(8, j);
+            issue_pv(0, sv, j);
+            if (lane == 0) FL_TRACE_EV(11, j);
+          }
+        }
       }
     }
     // Drain: wait until every MMA this thread issued has completed.
@@ -414,8 +431,14 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     float m_ref = -INFINITY;
     float l = 0.0f;
     bool ok = true;
+    // The two tiles run half a KV step apart, so that one warp of each SM
+    // sub-partition computes while the other waits on a barrier or a TMEM
+    // round trip: tile 0 signals half-way through its first tile and tile 1
+    // starts then.
+    bool stagger_sent = (i != 0);
+    if (i == 1 && my_nkv > 0) ok = warp_wait(bar_stagger, 0, abort_flag, p.err);
 
-    for (int j = 0; j < my_nkv; ++j) {
+    for (int j = 0; ok && j < my_nkv; ++j) {
       if (!warp_wait(bar_s(i), j & 1, abort_flag, p.err)) { ok = false; break; }
       if (t == 0) FL_TRACE_EV(0 + 4 * i, j);
       tc_fence_after();
@@ -520,6 +543,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
           pk[e] = pack_f16x2(pp.x, pp.y);
         }
         tmem_st16(tP + q * 16, pk);
+        if (q == 1 && !stagger_sent) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_stagger);
+          stagger_sent = true;
+        }
       }
       {
         const float2 a = __fadd2_rn(lsum[0], lsum[1]);
@@ -540,6 +568,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (lane == 0) mbar_arrive(bar_p(i));
       if (t == 0) FL_TRACE_EV(3 + 4 * i, j);
       if (t == 96) FL_TRACE_EV(14 + i, j);
+    }
+
+    if (!stagger_sent) {  // tile 0 without KV tiles, or stopped early
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_stagger);
     }
 
     // ---- epilogue ----

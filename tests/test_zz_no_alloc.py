@@ -12,6 +12,7 @@ allocated by a call; sizes beyond the array's 65536 rows are rejected.
 Collected last on purpose (file name), and independent of test order.
 """
 import ctypes
+import gc
 
 import pytest
 import torch
@@ -100,13 +101,15 @@ def test_call_allocates_no_device_memory(cuda, lib):
     o = torch.empty_like(q)
     _noalloc(lib, q, k, v, o, 0, 0, True, True, True)  # first call on the device: set-up
     torch.cuda.synchronize()
+    gc.collect()  # tensors of earlier tests still waiting for collection
     free0, _ = torch.cuda.mem_get_info()
     torch_alloc0 = torch.cuda.memory_allocated()
     for _ in range(3):
         _noalloc(lib, q, k, v, o, 0, 0, True, True, True)
     torch.cuda.synchronize()
     assert torch.cuda.mem_get_info()[0] == free0
-    assert torch.cuda.memory_allocated() == torch_alloc0
+    # torch may free (never allocate) blocks of earlier tests meanwhile
+    assert torch.cuda.memory_allocated() <= torch_alloc0
 
 
 def test_rejects_sizes_beyond_the_array(cuda, lib):
