@@ -72,6 +72,32 @@ def test_two_tiles_per_cta_dispatch(cuda, N, causal):
     _run(cuda, 4, 16, N, causal, seed=5)
 
 
+@pytest.mark.parametrize("B,H,N,causal", [
+    (1, 150, 200, False),   # 2 KV steps per CTA
+    (1, 150, 200, True),
+    (1, 160, 384, False),   # 3 query tiles: the second pair has one tile
+    (1, 160, 384, True),
+    (3, 50, 1000, True),    # causal pairs of 2..8 KV steps, ragged last tile
+])
+def test_many_two_tile_ctas(cuda, B, H, N, causal):
+    # >= 148 two-tile CTAs (more than one wave), short and odd-length cases
+    _run(cuda, B, H, N, causal, seed=B * H + N)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_repeatable_two_tile_dispatch(cuda, causal):
+    q, k, v = orc.make_qkv(4, 16, 1100, 64, seed=10)
+    ref = orc.attention_fp32(q, k, v, 0.125, causal)
+    qd, kd, vd = (t.to(cuda) for t in (q, k, v))
+    first = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+    for _ in range(3):
+        again = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+        assert torch.equal(first, again)
+    torch.cuda.synchronize()
+    assert fa.device_error() == 0
+    _check(first.cpu(), ref, "repeat")
+
+
 def test_default_and_negative_scale(cuda):
     _run(cuda, 1, 2, 256, False, seed=1, sm_scale=0.0)
     _run(cuda, 1, 2, 256, True, seed=2, sm_scale=-0.125)
