@@ -84,6 +84,21 @@ def test_many_two_tile_ctas(cuda, B, H, N, causal):
     _run(cuda, B, H, N, causal, seed=B * H + N)
 
 
+@pytest.mark.parametrize("B,H,N", [(2, 80, 1000), (1, 150, 256), (1, 148, 2048)])
+def test_full_pairs_many_ctas_repeatable(cuda, B, H, N):
+    # Non-causal, even query-tile count, >= 148 tile pairs (ragged keys and
+    # rows for N = 1000), run twice: the bits repeat.
+    q, k, v = orc.make_qkv(B, H, N, 64, seed=N + H)
+    ref = orc.attention_fp32(q, k, v, 0.125, False)
+    qd, kd, vd = (t.to(cuda) for t in (q, k, v))
+    a = fa.forward_flash2(qd, kd, vd, 0.125, False)
+    b = fa.forward_flash2(qd, kd, vd, 0.125, False)
+    torch.cuda.synchronize()
+    assert fa.device_error() == 0
+    assert torch.equal(a, b)
+    _check(a.cpu(), ref, f"B{B} H{H} N{N}")
+
+
 @pytest.mark.parametrize("causal", [False, True])
 def test_repeatable_two_tile_dispatch(cuda, causal):
     q, k, v = orc.make_qkv(4, 16, 1100, 64, seed=10)
