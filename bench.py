@@ -383,19 +383,24 @@ def run_ring(args):
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
     from flashlite_b200 import flash_attn_wmma as fa
-    from flashlite_b200.parallel_attn import RingAttention
+    from flashlite_b200.parallel_attn import RingAttention, ZigzagRingAttention
 
     B, H, N, causal, desc = WORKLOADS["cfg5"]
     D, sm_scale = 64, 0.125
-    assert N % world == 0
+    # causal rings use the zig-zag layout (rank r holds chunks r and 2P-1-r of
+    # 2P), which gives every rank the same work; --ring-layout contiguous keeps
+    # one contiguous block per rank
+    zigzag = world > 1 and causal and args.ring_layout == "zigzag"
+    assert N % (2 * world) == 0
     nb = N // world
+    shape = (2, B, H, nb // 2, D) if zigzag else (B, H, nb, D)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
-    q, k, v = ((torch.randn(B, H, nb, D, generator=g, device=device) * 0.5).to(torch.float16)
+    q, k, v = ((torch.randn(*shape, generator=g, device=device) * 0.5).to(torch.float16)
                for _ in range(3))
     out = torch.empty_like(q)
-    o_acc = torch.empty(B, H, nb, D, dtype=torch.float32, device=device)
-    lse = torch.empty(B, H, nb, dtype=torch.float32, device=device)
-    ring = RingAttention() if world > 1 else None
+    o_acc = torch.empty(*shape, dtype=torch.float32, device=device)
+    lse = torch.empty(*shape[:-1], dtype=torch.float32, device=device)
+    ring = (ZigzagRingAttention() if zigzag else RingAttention()) if world > 1 else None
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
 
     def step():
@@ -458,14 +463,17 @@ def run_ring(args):
             "data": "synthetic: seeded i.i.d. N(0,1)*0.5 fp16 Q/K/V generated per rank on device",
             "config": {"workload": desc, "B": B, "H": H, "N": N, "D": D, "causal": True,
                        "rows_per_rank": nb,
-                       "parallelism": f"ring x{world} (NCCL send/recv)" if world > 1 else "single GPU",
+                       "parallelism": (f"ring x{world} (NCCL send/recv), "
+                                       f"{'zig-zag' if zigzag else 'contiguous'} layout")
+                       if world > 1 else "single GPU",
                        "l2": "256 MiB buffer written between timed steps (untimed)"},
             "pct_of_peak": round(100 * per_gpu / peak_burst, 2),
             "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak_burst,
                          "unit": "TFLOP/s", "frac": round(per_gpu / peak_burst, 4),
                          "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
                          "traffic": None,
-                         "note": "per GPU; causal contiguous blocks cap the ideal ring speedup at P^2/(2P-1)"},
+                         "note": "per GPU" + ("; causal contiguous blocks cap the ideal ring speedup at P^2/(2P-1)"
+                                           if world > 1 and causal and not zigzag else "")},
             "e2e": {"value": round(total_flops / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
                     "ms_per_step": round(e_ms, 3)},
@@ -624,6 +632,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg3", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ring-layout", default="zigzag", choices=["zigzag", "contiguous"],
+                    help="sequence layout of the config-5 ring on 2+ GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -14,6 +14,11 @@ One process per GPU, ``torch.distributed`` for the plumbing.
   which folds the block's result into a running fp32 (O, log-sum-exp) state
   in its epilogue; with a causal mask, blocks from later ranks are skipped.
   A final cast writes fp16.
+* Zig-zag ring (causal): the sequence is cut into 2P chunks and rank r holds
+  chunks r and 2P-1-r, so every rank has the same causal work at every ring
+  step (contiguous blocks cap the causal speed-up at P²/(2P-1); zig-zag
+  removes the cap). Each step computes the visible (query chunk, key chunk)
+  pairs of the two local query chunks against the two received key chunks.
 """
 from __future__ import annotations
 
@@ -132,3 +137,78 @@ class RingAttention:
         self.finalize_fn(o_acc, out)
         return out
 
+
+
+def zigzag_chunks(rank: int, world: int) -> tuple:
+    """Chunk indices (of 2·world equal chunks) held by ``rank``."""
+    if world <= 0 or not (0 <= rank < world):
+        raise ValueError("invalid world/rank")
+    return rank, 2 * world - 1 - rank
+
+
+def zigzag_pairs(rank: int, src: int, world: int, causal: bool):
+    """(query chunk slot, key chunk slot) pairs to compute when ``rank`` holds
+    the key/value chunks of rank ``src``; slot 0 / 1 = the lower / upper chunk
+    of a rank. Pairs whose keys all lie after the queries are left out."""
+    qc, kc = zigzag_chunks(rank, world), zigzag_chunks(src, world)
+    return [(a, b) for a in range(2) for b in range(2) if not causal or kc[b] <= qc[a]]
+
+
+class ZigzagRingAttention(RingAttention):
+    """Ring attention over the zig-zag layout (see module docstring).
+
+    ``forward(q, k, v)`` takes this rank's two chunks as ``[2, B, H, c, D]``
+    tensors (slot 0 = chunk r, slot 1 = chunk 2P-1-r) and returns the output
+    in the same layout. The K/V of a rank travel as one contiguous
+    ``[2 (k, v), 2 (slots), B, H, c, D]`` buffer.
+    """
+
+    def _kv_buffers(self, kv: torch.Tensor):
+        key = (tuple(kv.shape), kv.dtype, kv.device, "zz")
+        if self._bufs is None or self._bufs[0] != key:
+            self._bufs = (key, [torch.empty_like(kv) for _ in range(2)])
+        return self._bufs[1]
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float = 0.0,
+                is_causal: bool = True, out: Optional[torch.Tensor] = None,
+                o_acc: Optional[torch.Tensor] = None,
+                lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        if q.shape != k.shape or k.shape != v.shape or q.dim() != 5 or q.shape[0] != 2:
+            raise ValueError("zig-zag ring attention expects q, k, v of shape [2, B, H, c, D]")
+        _, B, H, c, D = q.shape
+        if o_acc is None:
+            o_acc = torch.empty(2, B, H, c, D, dtype=torch.float32, device=q.device)
+        if lse is None:
+            lse = torch.empty(2, B, H, c, dtype=torch.float32, device=q.device)
+        if out is None:
+            out = torch.empty_like(q)
+        nxt, prv = (rank + 1) % world, (rank - 1) % world
+        g_nxt = dist.get_global_rank(self.group, nxt) if self.group is not None else nxt
+        g_prv = dist.get_global_rank(self.group, prv) if self.group is not None else prv
+        bufs = self._kv_buffers(torch.stack((k, v)))
+        cur = bufs[1]
+        cur.copy_(torch.stack((k, v)))
+        own = zigzag_chunks(rank, world)
+        started = [False, False]
+        for s in range(world):
+            src = (rank - s) % world
+            reqs = []
+            if s < world - 1:
+                nxt_buf = bufs[s % 2] if bufs[s % 2] is not cur else bufs[(s + 1) % 2]
+                ops = [dist.P2POp(dist.isend, cur, g_nxt, self.group),
+                       dist.P2POp(dist.irecv, nxt_buf, g_prv, self.group)]
+                reqs = dist.batch_isend_irecv(ops)
+            kc = zigzag_chunks(src, world)
+            for a, b in zigzag_pairs(rank, src, world, is_causal):
+                self.block_fn(q[a], cur[0, b], cur[1, b], o_acc[a], lse[a], own[a] * c, kc[b] * c,
+                              sm_scale, is_causal, not started[a])
+                started[a] = True
+            for r in reqs:
+                r.wait()
+            if s < world - 1:
+                cur = nxt_buf
+        for a in range(2):
+            self.finalize_fn(o_acc[a], out[a])
+        return out

@@ -1,4 +1,5 @@
-"""Head sharding and ring attention on 2+ GPUs over NCCL (one process per GPU).
+"""Head sharding, ring and zig-zag ring attention on 2+ GPUs over NCCL (one
+process per GPU).
 
 The CPU suite covers the same host logic with gloo ranks
 (test_parallel_cpu.py); this file runs the CUDA kernels with real NCCL
@@ -34,7 +35,8 @@ def _worker(rank, world, port, causal, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=dev)
     try:
-        from flashlite_b200.parallel_attn import RingAttention, head_sharded_forward, shard_range
+        from flashlite_b200.parallel_attn import (RingAttention, ZigzagRingAttention,
+                                                  head_sharded_forward, shard_range, zigzag_chunks)
 
         q, k, v = (t.to(dev) for t in orc.make_qkv(1, H, N, D, seed=31))
         nb = N // world
@@ -46,9 +48,14 @@ def _worker(rank, world, port, causal, results):
         heads = shard_range(H, world, rank)
         hs = [t[:, heads.start:heads.stop].contiguous() for t in (q, k, v)]
         head_out = head_sharded_forward(*hs, 0.125, causal)
+        # zig-zag layout: chunks r and 2P-1-r of 2P
+        c = N // (2 * world)
+        own = zigzag_chunks(rank, world)
+        zz = [torch.stack([t[:, :, i * c:(i + 1) * c] for i in own]).contiguous() for t in (q, k, v)]
+        zz_out = ZigzagRingAttention().forward(*zz, 0.125, causal)
         torch.cuda.synchronize()
         dist.barrier()
-        results.put((rank, ring_out.cpu(), ring_out2.cpu(), head_out.cpu()))
+        results.put((rank, ring_out.cpu(), ring_out2.cpu(), head_out.cpu(), zz_out.cpu()))
     finally:
         dist.destroy_process_group()
 
@@ -70,8 +77,8 @@ def test_ring_and_head_sharding_match_oracle(causal):
     got = {}
     try:
         for _ in range(world):
-            rank, a, b, c = results.get(timeout=240)
-            got[rank] = (a, b, c)
+            rank, a, b, c, z = results.get(timeout=240)
+            got[rank] = (a, b, c, z)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -80,7 +87,11 @@ def test_ring_and_head_sharding_match_oracle(causal):
     q, k, v = orc.make_qkv(1, H, N, D, seed=31)
     ref = orc.attention_fp32(q, k, v, 0.125, causal)
     nb = N // world
-    for rank, (ring_out, ring_out2, head_out) in got.items():
+    cz = N // (2 * world)
+    for rank, (ring_out, ring_out2, head_out, zz_out) in got.items():
+        for a, ch in enumerate((rank, 2 * world - 1 - rank)):
+            mx, mean = orc.error_metrics(zz_out[a], ref[:, :, ch * cz:(ch + 1) * cz])
+            assert mx <= orc.MAX_ABS_TOL and mean <= orc.MEAN_ABS_TOL, ("zigzag", rank, a, mx, mean)
         want = ref[:, :, rank * nb:(rank + 1) * nb]
         mx, mean = orc.error_metrics(ring_out, want)
         assert mx <= orc.MAX_ABS_TOL and mean <= orc.MEAN_ABS_TOL, (rank, mx, mean)

@@ -4,6 +4,8 @@
 * ring attention: RingAttention's schedule, double-buffered send/recv and
   merge order, run on world sizes 2 and 4 with a host implementation of the
   block step, reproduce full attention of every rank's query block;
+* zig-zag ring: every rank holds chunks r and 2P-1-r, computes the same
+  number of key blocks, and reproduces full attention of its two chunks;
 * failure: a rank that raises before the ring leaves the others with an
   error from the process group's timeout, not a hang.
 """
@@ -17,7 +19,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from flashlite_b200.parallel_attn import RingAttention, ring_schedule, shard_range
+from flashlite_b200.parallel_attn import (RingAttention, ZigzagRingAttention, ring_schedule,
+                                          shard_range, zigzag_chunks, zigzag_pairs)
 from oracle.attention_oracle import attention_fp32, block_attention_lse, merge_lse
 
 
@@ -51,6 +54,58 @@ def test_ring_schedule():
     assert ring_schedule(0, 4, True) == [(0, True), (3, False), (2, False), (1, False)]
     assert ring_schedule(2, 4, True) == [(2, True), (1, True), (0, True), (3, False)]
     assert all(c for _, c in ring_schedule(1, 3, False))
+
+
+def test_zigzag_schedule_is_balanced():
+    for world in (2, 4, 8):
+        assert sorted(c for r in range(world) for c in zigzag_chunks(r, world)) == list(range(2 * world))
+        work = []
+        for r in range(world):
+            pairs = [zigzag_pairs(r, (r - s) % world, world, True) for s in range(world)]
+            assert all(len(p) == 2 for p in pairs[1:])   # equal work at every later step
+            work.append(sum(len(p) for p in pairs))
+        assert len(set(work)) == 1
+        assert all(len(zigzag_pairs(r, s, world, False)) == 4 for r in range(world) for s in range(world))
+
+
+def _zigzag_worker(rank, world, port, causal, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=30))
+        torch.manual_seed(0)
+        c, H, D = 12, 2, 16
+        q, k, v = (torch.randn(1, H, 2 * world * c, D) for _ in range(3))
+        full = attention_fp32(q, k, v, 0.25, causal)
+        own = zigzag_chunks(rank, world)
+        pick = lambda t: torch.stack([t[:, :, i * c:(i + 1) * c] for i in own]).contiguous()
+        ring = ZigzagRingAttention(block_fn=cpu_block_fn, finalize_fn=cpu_finalize_fn)
+        out = ring.forward(pick(q), pick(k), pick(v), 0.25, causal)
+        out2 = ring.forward(pick(q), pick(k), pick(v), 0.25, causal)  # buffers reused
+        err = max((out - pick(full)).abs().max().item(), (out2 - out).abs().max().item())
+        results[rank] = err
+        dist.destroy_process_group()
+    except Exception:  # report, never hang the parent
+        results[rank] = traceback.format_exc()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("causal", [True, False])
+def test_zigzag_ring_attention_gloo(world, causal):
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_zigzag_worker, args=(r, world, port, causal, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0, "zig-zag ring worker did not finish"
+    for r in range(world):
+        assert isinstance(results[r], float), results[r]
+        assert results[r] < 1e-5, (r, results[r])
 
 
 def _free_port():

@@ -76,6 +76,34 @@ def test_ring_emulation_equals_full_attention(cuda, P, causal):
         assert mx <= orc.MAX_ABS_TOL and mean <= orc.MEAN_ABS_TOL, (r, mx, mean)
 
 
+@pytest.mark.parametrize("P", [2, 4])
+def test_zigzag_ring_emulation_equals_full_attention(cuda, P):
+    """The zig-zag layout's block schedule (ZigzagRingAttention without the
+    communication): rank r's two chunks against every rank's chunk pairs."""
+    from flashlite_b200.parallel_attn import zigzag_chunks, zigzag_pairs
+
+    c, H = 192, 2
+    q, k, v = orc.make_qkv(1, H, 2 * P * c, 64, seed=10 + P)
+    full = orc.attention_fp32(q, k, v, 0.125, True)
+    chunk = lambda t, i: t[:, :, i * c:(i + 1) * c].contiguous()
+    for r in range(P):
+        own = zigzag_chunks(r, P)
+        acc = [None, None]
+        for s in range(P):
+            src = (r - s) % P
+            kc = zigzag_chunks(src, P)
+            for a, b in zigzag_pairs(r, src, P, True):
+                o_acc, lse = acc[a] if acc[a] is not None else (None, None)
+                acc[a] = _block(cuda, chunk(q, own[a]), chunk(k, kc[b]), chunk(v, kc[b]),
+                                own[a] * c, kc[b] * c, True, o_acc, lse, first=acc[a] is None)
+        for a in range(2):
+            out = torch.empty(1, H, c, 64, dtype=torch.float16, device=cuda)
+            fa.ring_finalize(acc[a][0], out)
+            torch.cuda.synchronize()
+            mx, mean = orc.error_metrics(out.cpu(), chunk(full, own[a]))
+            assert mx <= orc.MAX_ABS_TOL and mean <= orc.MEAN_ABS_TOL, (r, a, mx, mean)
+
+
 @pytest.mark.slow
 def test_config5_shape_sampled_rows(cuda):
     """BASELINE config 5 (B1 H8 N131072, inputs N(0,1)*0.5, causal) with 1 head,
