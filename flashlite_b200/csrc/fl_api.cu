@@ -149,6 +149,31 @@ int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t 
   return FL_OK;
 }
 
+int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
+                     int64_t H, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
+                     int64_t kv_offset, float sm_scale, int is_causal, void* stream) {
+  if (!q || !k || !v || !o) return fail(FL_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (B < 0 || H < 0 || Nq < 0 || Nk < 0 || D < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative size");
+  if (Nq > (1LL << 30) || Nk > (1LL << 30) || B * H > (1LL << 30))
+    return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
+  if (q_offset < 0 || kv_offset < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative offset");
+  if (D != 64) return fail(FL_ERR_UNSUPPORTED, "FlashLite WMMA kernel currently requires head_dim == 64");
+  if (B == 0 || H == 0 || Nq == 0) return FL_OK;
+  if (Nk == 0) return fail(FL_ERR_INVALID_ARGUMENT, "empty key sequence");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(FL_ERR_MISALIGNED, "q, k, v and out must be 16-byte aligned");
+  int st = check_device();
+  if (st != FL_OK) return st;
+  double scale = sm_scale;
+  if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
+  const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
+  cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, lse, B * H, Nq, Nk, q_offset, kv_offset,
+                                    scale_log2, is_causal != 0, false, false,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "flash2 launch");
+  return FL_OK;
+}
+
 int fl_naive_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
                  int64_t N, int64_t D, float sm_scale, int is_causal, void* stream) {
   int st = check_common(q, k, v, o, B, H, N, D);

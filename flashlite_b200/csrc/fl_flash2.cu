@@ -591,7 +591,20 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     }
     const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
     if (!kMerge) {
-      if (do_out) {
+      // A tile whose rows see no key at all (key positions offset past the
+      // queries) is written as zeros, as fully masked rows are.
+      const bool write = active && ok;
+      if (write && !do_out) {
+        // The staging buffer is this tile's Q buffer: let its load land first
+        // (with no KV step nothing else waited for it).
+        warp_wait(bar_q, 0, abort_flag, p.err);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) o[c] = 0u;
+      }
+      if (p.lse != nullptr && write && q_start + t < p.nq)
+        p.lse[static_cast<long long>(bh) * p.nq + q_start + t] =
+            (l > 0.0f) ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
+      if (write) {
         // Stage the fp16 tile in the (now unused) Q buffer with the 128B
         // swizzle the TMA store expects: 16-byte chunk c of row t goes to
         // chunk position c ^ (t % 8).
@@ -608,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         fence_proxy_async_smem();
       }
       named_bar_sync(1 + i, 128);
-      if (do_out && t == 0 && !*abort_flag) {
+      if (write && t == 0 && !*abort_flag) {
         tma_store_3d(&p.tm_o, s_q[i], 0, q_start, bh);
         tma_store_commit();
         tma_store_wait_read0();

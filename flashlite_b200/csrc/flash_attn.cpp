@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 
 #include <optional>
+#include <vector>
 
 #include "../../include/flashlite_b200.h"
 
@@ -99,6 +100,48 @@ torch::Tensor forward_naive(torch::Tensor q, torch::Tensor k, torch::Tensor v, d
 // One ring-attention block step (no reference counterpart): merges
 // attention of q [B,H,Nq,64] against k/v [B,H,Nk,64] into (o_acc fp32
 // [B,H,Nq,64], lse fp32 [B,H,Nq]).
+// Extension without a reference counterpart: N_k != N_q, position offsets,
+// optional LSE output (fl_flash2_fwd_ex). Returns (out, lse); lse is an
+// empty tensor unless return_lse.
+std::vector<torch::Tensor> forward_flash2_ex(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                             double sm_scale, bool is_causal, int64_t q_offset,
+                                             int64_t kv_offset, std::optional<torch::Tensor> out,
+                                             bool return_lse) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "All tensors must be on CUDA");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
+              "All tensors must be contiguous");
+  TORCH_CHECK(q.dtype() == torch::kHalf && k.dtype() == torch::kHalf && v.dtype() == torch::kHalf,
+              "All tensors must be FP16 (Half)");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Tensors must be 4D [B, H, N, D]");
+  const int64_t B = q.size(0), H = q.size(1), Nq = q.size(2), D = q.size(3), Nk = k.size(2);
+  TORCH_CHECK(k.size(0) == B && k.size(1) == H && k.size(3) == D,
+              "Key dimensions must match Query dimensions [B, H, N_k, D]");
+  TORCH_CHECK(v.sizes() == k.sizes(), "Value dimensions must match Key dimensions [B, H, N_k, D]");
+  TORCH_CHECK(D == 64, "FlashLite WMMA kernel currently requires head_dim == 64");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
+              "All tensors must be on the same CUDA device");
+  torch::Tensor out_tensor;
+  if (out.has_value() && out.value().defined()) {
+    out_tensor = out.value();
+    TORCH_CHECK(out_tensor.is_cuda() && out_tensor.is_contiguous(),
+                "out tensor must be contiguous CUDA tensor");
+    TORCH_CHECK(out_tensor.sizes() == q.sizes(), "out tensor shape must match q");
+    TORCH_CHECK(out_tensor.dtype() == torch::kHalf, "out tensor dtype must be FP16");
+    TORCH_CHECK(out_tensor.device() == q.device(), "out tensor must be on the same device as q");
+  } else {
+    out_tensor = torch::empty_like(q);
+  }
+  torch::Tensor lse = return_lse ? torch::empty({B, H, Nq}, q.options().dtype(torch::kFloat32))
+                                 : torch::empty({0}, q.options().dtype(torch::kFloat32));
+  if (out_tensor.numel() == 0) return {out_tensor, lse};
+  const c10::cuda::CUDAGuard guard(q.device());
+  check_status(fl_flash2_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_tensor.data_ptr(),
+                                return_lse ? lse.data_ptr<float>() : nullptr, B, H, Nq, Nk, D,
+                                q_offset, kv_offset, static_cast<float>(sm_scale), is_causal ? 1 : 0,
+                                stream_of(q)));
+  return {out_tensor, lse};
+}
+
 void forward_block(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o_acc,
                    torch::Tensor lse, int64_t q_offset, int64_t kv_offset, double sm_scale,
                    bool is_causal, bool first) {
@@ -155,6 +198,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_flash2", &forward_flash2, "FlashAttention-2 forward (tcgen05, sm_100a)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("sm_scale") = 0.0,
         py::arg("is_causal") = false, py::arg("out") = py::none());
+  m.def("forward_flash2_ex", &forward_flash2_ex,
+        "FA2 forward with N_k != N_q, position offsets and optional LSE; returns (out, lse)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("sm_scale") = 0.0,
+        py::arg("is_causal") = false, py::arg("q_offset") = 0, py::arg("kv_offset") = 0,
+        py::arg("out") = py::none(), py::arg("return_lse") = false);
   m.def("forward_block", &forward_block, "Ring-attention block step with LSE merge",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o_acc"), py::arg("lse"),
         py::arg("q_offset"), py::arg("kv_offset"), py::arg("sm_scale") = 0.0,

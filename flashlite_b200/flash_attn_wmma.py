@@ -15,20 +15,26 @@ functions are the C++ binding's own (``flashlite_b200._C``); there is no
 Python or CPU fallback: importing this module without the built native code
 raises ImportError.
 
-Extra entry points (no reference counterpart) used by ring attention:
-``forward_block`` and ``ring_finalize``; ``device_error`` reads the error
-bits kernels raise when a bounded wait gives up.
+Extra entry points (no reference counterpart):
+``forward_flash2_ex(q, k, v, sm_scale=0.0, is_causal=False, q_offset=0,
+kv_offset=0, out=None, return_lse=False) -> (out, lse)`` takes N_k != N_q
+and global positions (query row i at q_offset + i, key row j at
+kv_offset + j) and can return the per-row log-sum-exp; ``forward_block`` and
+``ring_finalize`` are the ring-attention steps; ``device_error`` reads the
+error bits kernels raise when a bounded wait gives up.
 """
 from __future__ import annotations
 
 import torch  # noqa: F401  (loads libtorch/libc10 for the binding)
 
 try:
-    from ._C import device_error, forward_block, forward_flash2, forward_naive, ring_finalize
+    from ._C import (device_error, forward_block, forward_flash2, forward_flash2_ex,
+                     forward_naive, ring_finalize)
 except ImportError as exc:  # pragma: no cover - exercised only on unbuilt trees
     raise ImportError(
         "flashlite_b200 native extension is not built; run `python -m flashlite_b200.build` "
         f"(or __graft_entry__.build()): {exc}"
     ) from exc
 
-__all__ = ["forward_flash2", "forward_naive", "forward_block", "ring_finalize", "device_error"]
+__all__ = ["forward_flash2", "forward_naive", "forward_flash2_ex", "forward_block", "ring_finalize",
+           "device_error"]
