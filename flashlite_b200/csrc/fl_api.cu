@@ -143,16 +143,19 @@ int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t 
   double scale = sm_scale;
   if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
-  cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, nullptr, B * H, N, N, 0, 0, scale_log2,
-                                    is_causal != 0, false, false, static_cast<cudaStream_t>(stream));
+  cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, nullptr, B, H, N, N, 0, 0, scale_log2,
+                                    is_causal != 0, false, false, false,
+                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "flash2 launch");
   return FL_OK;
 }
 
 int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
                      int64_t H, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
-                     int64_t kv_offset, float sm_scale, int is_causal, void* stream) {
+                     int64_t kv_offset, float sm_scale, int is_causal, int layout, void* stream) {
   if (!q || !k || !v || !o) return fail(FL_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (layout != FL_LAYOUT_BHND && layout != FL_LAYOUT_BNHD)
+    return fail(FL_ERR_INVALID_ARGUMENT, "unknown layout");
   if (B < 0 || H < 0 || Nq < 0 || Nk < 0 || D < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative size");
   if (Nq > (1LL << 30) || Nk > (1LL << 30) || B * H > (1LL << 30))
     return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
@@ -167,9 +170,9 @@ int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float
   double scale = sm_scale;
   if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
-  cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, lse, B * H, Nq, Nk, q_offset, kv_offset,
+  cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, lse, B, H, Nq, Nk, q_offset, kv_offset,
                                     scale_log2, is_causal != 0, false, false,
-                                    static_cast<cudaStream_t>(stream));
+                                    layout == FL_LAYOUT_BNHD, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "flash2 launch");
   return FL_OK;
 }
@@ -209,8 +212,8 @@ int fl_flash2_fwd_block(const void* q, const void* k, const void* v, float* o_ac
   double scale = sm_scale;
   if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
-  cudaError_t e = fl::launch_flash2(q, k, v, nullptr, o_acc, lse, BH, Nq, Nk, q_offset, kv_offset,
-                                    scale_log2, is_causal != 0, true, first != 0,
+  cudaError_t e = fl::launch_flash2(q, k, v, nullptr, o_acc, lse, 1, BH, Nq, Nk, q_offset,
+                                    kv_offset, scale_log2, is_causal != 0, true, first != 0, false,
                                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "flash2 block launch");
   return FL_OK;

@@ -110,15 +110,19 @@ constexpr int kSmemBytes = kSmemMisc + 16;
 constexpr int kSmemAlloc = kSmemBytes + 1024;              // alignment slack
 
 struct Flash2Params {
-  CUtensorMap tm_q;  // {64, Nq, BH} fp16, box {64, 128, 1}, SW128
-  CUtensorMap tm_k;  // {64, Nk, BH}
-  CUtensorMap tm_v;  // {64, Nk, BH}
-  CUtensorMap tm_o;  // {64, Nq, BH} (unused in merge mode)
+  // 4-D maps {64, rows, H, B} with box {64, 128, 1, 1}, SW128; the strides
+  // give the [B,H,N,D] or [B,N,H,D] layout, the kernel's coordinates are the
+  // same for both: (0, row, h, b).
+  CUtensorMap tm_q;  // {64, Nq, H, B} fp16
+  CUtensorMap tm_k;  // {64, Nk, H, B}
+  CUtensorMap tm_v;  // {64, Nk, H, B}
+  CUtensorMap tm_o;  // {64, Nq, H, B} (unused in merge mode)
   float* o_acc;      // merge mode: [BH, Nq, 64] fp32
   float* lse;        // merge mode: [BH, Nq] fp32 (natural log)
   unsigned int* err; // device error word
   int nq, nk;        // query / key rows per slice
   int bh;            // number of (b,h) slices
+  int nh;            // heads per batch entry: slice bh is (b, h) = (bh / nh, bh % nh)
   int n_qtiles;      // ceil(nq / 128)
   int n_ktiles;      // ceil(nk / 128)
   int tiles_per_cta; // 1 or 2 query tiles per CTA
@@ -173,7 +177,7 @@ __device__ long long fl_trace_buf[kTraceEvents * kTraceIters];
 // the consumer released that stage. Returns the number of tiles issued.
 template <int kStages>
 __device__ __forceinline__ int produce_ring(const CUtensorMap* tm, uint32_t s_ring, uint32_t bar_full0,
-                                            uint32_t bar_empty0, int n_tiles, int bh, int lane,
+                                            uint32_t bar_empty0, int n_tiles, int h, int b, int lane,
                                             volatile int* abort_flag, unsigned int* err) {
   int issued = 0;
   for (int t = 0; t < n_tiles; ++t) {
@@ -182,7 +186,7 @@ __device__ __forceinline__ int produce_ring(const CUtensorMap* tm, uint32_t s_ri
     if (!warp_wait(bar_empty0 + 8u * st, ph ^ 1, abort_flag, err)) break;
     if (lane == 0) {
       mbar_arrive_expect_tx(bar_full0 + 8u * st, kTileBytes);
-      tma_load_3d(s_ring + st * kTileBytes, tm, bar_full0 + 8u * st, 0, t * kBN, bh);
+      tma_load_4d(s_ring + st * kTileBytes, tm, bar_full0 + 8u * st, 0, t * kBN, h, b);
     }
     __syncwarp();
     issued = t + 1;
@@ -286,12 +290,12 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_k);
       mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kTileBytes);
-      tma_load_3d(s_q[0], &p.tm_q, bar_q, 0, qt0 * kBM, bh);
-      if (has_q1) tma_load_3d(s_q[1], &p.tm_q, bar_q, 0, (qt0 + 1) * kBM, bh);
+      tma_load_4d(s_q[0], &p.tm_q, bar_q, 0, qt0 * kBM, bh % p.nh, bh / p.nh);
+      if (has_q1) tma_load_4d(s_q[1], &p.tm_q, bar_q, 0, (qt0 + 1) * kBM, bh % p.nh, bh / p.nh);
     }
     __syncwarp();
-    const int issued = produce_ring<kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv, bh,
-                                              lane, abort_flag, p.err);
+    const int issued = produce_ring<kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv,
+                                              bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) {
       // Drain: let every copy this CTA started land before shared memory is released.
       mbar_wait_quiet(bar_q, 0);
@@ -300,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   } else if (warp == 2) {
     // ======================= V producer =======================
     if (lane == 0) tma_prefetch_desc(&p.tm_v);
-    const int issued = produce_ring<kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv, bh,
-                                              lane, abort_flag, p.err);
+    const int issued = produce_ring<kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv,
+                                              bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
@@ -622,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       }
       named_bar_sync(1 + i, 128);
       if (write && t == 0 && !*abort_flag) {
-        tma_store_3d(&p.tm_o, s_q[i], 0, q_start, bh);
+        tma_store_4d(&p.tm_o, s_q[i], 0, q_start, bh % p.nh, bh / p.nh);
         tma_store_commit();
         tma_store_wait_read0();
       }
@@ -701,17 +705,27 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// Tensor map over a [slices, rows, 64] fp16 array with a {64, 128, 1} box.
-bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t slices) {
+// Tensor map {64, rows, H, B} over a [B,H,rows,64] (bnhd = false) or
+// [B,rows,H,64] (bnhd = true) fp16 array, box {64, 128, 1, 1}.
+bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H, int64_t B,
+                     bool bnhd) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows),
-                        static_cast<cuuint64_t>(slices)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD * 2),
-                           static_cast<cuuint64_t>(rows) * kD * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kBM), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+  const cuuint64_t row_b = kD * 2;  // bytes of one 64-wide fp16 row
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3];
+  if (!bnhd) {
+    strides[0] = row_b;                                       // next row
+    strides[1] = static_cast<cuuint64_t>(rows) * row_b;       // next head
+  } else {
+    strides[0] = static_cast<cuuint64_t>(H) * row_b;          // next row
+    strides[1] = row_b;                                       // next head
+  }
+  strides[2] = static_cast<cuuint64_t>(rows) * H * row_b;     // next batch entry
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kBM), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -735,19 +749,22 @@ cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t strea
 }  // namespace
 
 cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
-                          float* lse, int64_t BH, int64_t Nq, int64_t Nk, int64_t q_offset,
-                          int64_t kv_offset, float scale_log2, bool causal, bool merge,
-                          bool first, cudaStream_t stream) {
+                          float* lse, int64_t B, int64_t H, int64_t Nq, int64_t Nk,
+                          int64_t q_offset, int64_t kv_offset, float scale_log2, bool causal,
+                          bool merge, bool first, bool bnhd, cudaStream_t stream) {
   Flash2Params prm;
-  if (!encode_rows_map(&prm.tm_q, q, Nq, BH) || !encode_rows_map(&prm.tm_k, k, Nk, BH) ||
-      !encode_rows_map(&prm.tm_v, v, Nk, BH)) {
+  const int64_t BH = B * H;
+  if (!encode_rows_map(&prm.tm_q, q, Nq, H, B, bnhd) ||
+      !encode_rows_map(&prm.tm_k, k, Nk, H, B, bnhd) ||
+      !encode_rows_map(&prm.tm_v, v, Nk, H, B, bnhd)) {
     return cudaErrorInvalidValue;
   }
   if (!merge) {
-    if (!encode_rows_map(&prm.tm_o, o_f16, Nq, BH)) return cudaErrorInvalidValue;
+    if (!encode_rows_map(&prm.tm_o, o_f16, Nq, H, B, bnhd)) return cudaErrorInvalidValue;
   } else {
     prm.tm_o = prm.tm_q;
   }
+  prm.nh = static_cast<int>(H);
   prm.o_acc = o_acc;
   prm.lse = lse;
   prm.err = device_error_word();

@@ -103,8 +103,8 @@ extern "C" int fl_flash2_fwd_block_noalloc(const void* q, const void* k, const v
   if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = fl::launch_flash2(q, k, v, nullptr, o_acc, lse, BH, Nq, Nk, q_offset, kv_offset,
-                                    scale_log2, is_causal != 0, true, first != 0, s);
+  cudaError_t e = fl::launch_flash2(q, k, v, nullptr, o_acc, lse, 1, BH, Nq, Nk, q_offset,
+                                    kv_offset, scale_log2, is_causal != 0, true, first != 0, false, s);
   if (e != cudaSuccess) return fail(FL_ERR_CUDA, std::string("block launch: ") + cudaGetErrorString(e));
   if (last) {
     e = fl::launch_ring_finalize(o_acc, o, BH * Nq * kHeadDim, s);

@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 
 #include <optional>
+#include <string>
 #include <vector>
 
 #include "../../include/flashlite_b200.h"
@@ -106,16 +107,21 @@ torch::Tensor forward_naive(torch::Tensor q, torch::Tensor k, torch::Tensor v, d
 std::vector<torch::Tensor> forward_flash2_ex(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                              double sm_scale, bool is_causal, int64_t q_offset,
                                              int64_t kv_offset, std::optional<torch::Tensor> out,
-                                             bool return_lse) {
+                                             bool return_lse, std::string layout) {
+  TORCH_CHECK(layout == "bhnd" || layout == "bnhd", "layout must be 'bhnd' or 'bnhd'");
+  const bool bnhd = layout == "bnhd";
   TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "All tensors must be on CUDA");
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
               "All tensors must be contiguous");
   TORCH_CHECK(q.dtype() == torch::kHalf && k.dtype() == torch::kHalf && v.dtype() == torch::kHalf,
               "All tensors must be FP16 (Half)");
-  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "Tensors must be 4D [B, H, N, D]");
-  const int64_t B = q.size(0), H = q.size(1), Nq = q.size(2), D = q.size(3), Nk = k.size(2);
-  TORCH_CHECK(k.size(0) == B && k.size(1) == H && k.size(3) == D,
-              "Key dimensions must match Query dimensions [B, H, N_k, D]");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4,
+              bnhd ? "Tensors must be 4D [B, N, H, D]" : "Tensors must be 4D [B, H, N, D]");
+  const int hd = bnhd ? 2 : 1, nd = bnhd ? 1 : 2;  // dimension of heads / rows
+  const int64_t B = q.size(0), H = q.size(hd), Nq = q.size(nd), D = q.size(3), Nk = k.size(nd);
+  TORCH_CHECK(k.size(0) == B && k.size(hd) == H && k.size(3) == D,
+              bnhd ? "Key dimensions must match Query dimensions [B, N_k, H, D]"
+                   : "Key dimensions must match Query dimensions [B, H, N_k, D]");
   TORCH_CHECK(v.sizes() == k.sizes(), "Value dimensions must match Key dimensions [B, H, N_k, D]");
   TORCH_CHECK(D == 64, "FlashLite WMMA kernel currently requires head_dim == 64");
   TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
@@ -138,7 +144,7 @@ std::vector<torch::Tensor> forward_flash2_ex(torch::Tensor q, torch::Tensor k, t
   check_status(fl_flash2_fwd_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_tensor.data_ptr(),
                                 return_lse ? lse.data_ptr<float>() : nullptr, B, H, Nq, Nk, D,
                                 q_offset, kv_offset, static_cast<float>(sm_scale), is_causal ? 1 : 0,
-                                stream_of(q)));
+                                bnhd ? FL_LAYOUT_BNHD : FL_LAYOUT_BHND, stream_of(q)));
   return {out_tensor, lse};
 }
 
@@ -202,7 +208,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "FA2 forward with N_k != N_q, position offsets and optional LSE; returns (out, lse)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("sm_scale") = 0.0,
         py::arg("is_causal") = false, py::arg("q_offset") = 0, py::arg("kv_offset") = 0,
-        py::arg("out") = py::none(), py::arg("return_lse") = false);
+        py::arg("out") = py::none(), py::arg("return_lse") = false, py::arg("layout") = "bhnd");
   m.def("forward_block", &forward_block, "Ring-attention block step with LSE merge",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o_acc"), py::arg("lse"),
         py::arg("q_offset"), py::arg("kv_offset"), py::arg("sm_scale") = 0.0,

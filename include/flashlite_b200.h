@@ -43,20 +43,28 @@ typedef enum fl_status {
 int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
                   int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);
 
+/* Tensor layouts accepted by fl_flash2_fwd_ex. */
+enum fl_layout {
+  FL_LAYOUT_BHND = 0, /* [B, H, N, D]: the reference's layout */
+  FL_LAYOUT_BNHD = 1  /* [B, N, H, D]: the flash_attn package's layout */
+};
+
 /*
- * FA2 forward with separate query / key lengths, global positions and an
- * optional log-sum-exp output; no reference counterpart (the reference's
- * forward_flash2 assumes N_k == N_q without checking it,
- * csrc/kernel_flash2.cu:749-755). q, o: [B, H, Nq, 64] fp16; k, v:
- * [B, H, Nk, 64] fp16. Query row i sits at position q_offset + i and key
- * row j at kv_offset + j; with is_causal a query sees the keys at positions
- * <= its own. lse (may be NULL): [B, H, Nq] fp32, natural-log log-sum-exp of
- * the scaled scores of each row (-inf for a row without visible keys, whose
- * output is zero). sm_scale == 0 means 1/sqrt(64).
+ * FA2 forward with separate query / key lengths, global positions, an
+ * optional log-sum-exp output and a choice of layout; no reference
+ * counterpart (the reference's forward_flash2 assumes N_k == N_q without
+ * checking it, csrc/kernel_flash2.cu:749-755, and takes [B, H, N, D] only).
+ * q, o: [B, H, Nq, 64] (or [B, Nq, H, 64] with FL_LAYOUT_BNHD) fp16; k, v:
+ * [B, H, Nk, 64] (or [B, Nk, H, 64]) fp16. Query row i sits at position
+ * q_offset + i and key row j at kv_offset + j; with is_causal a query sees
+ * the keys at positions <= its own. lse (may be NULL): [B, H, Nq] fp32 in
+ * either layout, natural-log log-sum-exp of the scaled scores of each row
+ * (-inf for a row without visible keys, whose output is zero).
+ * sm_scale == 0 means 1/sqrt(64).
  */
 int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
                      int64_t H, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
-                     int64_t kv_offset, float sm_scale, int is_causal, void* stream);
+                     int64_t kv_offset, float sm_scale, int is_causal, int layout, void* stream);
 
 /*
  * Naive (unfused, fp32 CUDA-core) attention forward, any D in [1, 1024].

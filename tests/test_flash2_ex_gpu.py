@@ -69,3 +69,28 @@ def test_out_buffer_and_errors(cuda):
         fa.forward_flash2_ex(q, k, v, 0.125, True, -1, 0)
     with pytest.raises(RuntimeError, match="Value dimensions must match Key"):
         fa.forward_flash2_ex(q, k, v[:, :, :128].contiguous())
+
+
+@pytest.mark.parametrize("B,H,N,causal", [(2, 8, 1024, False), (2, 8, 1024, True), (4, 40, 1000, True),
+                                          (1, 3, 200, False)])
+def test_bnhd_layout_equals_bhnd(cuda, B, H, N, causal):
+    # [B, N, H, D] (the flash_attn package's layout) through 4-D tensor maps:
+    # the same arithmetic as [B, H, N, D], so the bits must agree
+    q, k, v = (t.to(cuda) for t in orc.make_qkv(B, H, N, 64, seed=N + H))
+    ref = fa.forward_flash2(q, k, v, 0.125, causal)
+    qt, kt, vt = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+    out, lse = fa.forward_flash2_ex(qt, kt, vt, 0.125, causal, return_lse=True, layout="bnhd")
+    _, lse_ref = fa.forward_flash2_ex(q, k, v, 0.125, causal, return_lse=True)
+    torch.cuda.synchronize()
+    assert out.shape == (B, N, H, 64) and lse.shape == (B, H, N)
+    assert torch.equal(out.transpose(1, 2), ref)
+    assert torch.equal(lse, lse_ref)
+
+
+def test_bnhd_rejects_mismatched_shapes(cuda):
+    q = torch.zeros(1, 128, 2, 64, dtype=torch.float16, device=cuda)
+    k = torch.zeros(1, 128, 3, 64, dtype=torch.float16, device=cuda)
+    with pytest.raises(RuntimeError, match=r"\[B, N_k, H, D\]"):
+        fa.forward_flash2_ex(q, k, k, layout="bnhd")
+    with pytest.raises(RuntimeError, match="layout must be"):
+        fa.forward_flash2_ex(q, q, q, layout="nhd")
