@@ -50,6 +50,22 @@ def test_two_tile_dispatch_with_lse(cuda):
     _case(cuda, 4, 40, 1024, 768, 256, 0, True, seed=9)
 
 
+@pytest.mark.parametrize("B,H,Nq,Nk", [
+    (1, 160, 256, 100),    # one KV step per unit: every CTA share is whole units or one-step cuts
+    (2, 80, 1000, 1000),   # ragged rows and keys, units cut between CTAs
+    (1, 150, 512, 3000),   # more keys than queries
+])
+def test_full_pairs_many_ctas_with_lse(cuda, B, H, Nq, Nk):
+    # non-causal, even query-tile count, >= 148 tile pairs: the persistent
+    # launch, whose cut units merge (O, m, l) parts; LSE from the merged parts
+    a, lse_a = _case(cuda, B, H, Nq, Nk, 0, 0, False, seed=Nq + H)
+    q, _, _ = orc.make_qkv(B, H, Nq, 64, seed=Nq + H)
+    _, k, v = orc.make_qkv(B, H, Nk, 64, seed=Nq + H + 1)
+    b = fa.forward_flash2_ex(q.to(cuda), k.to(cuda), v.to(cuda), 0.125, False)[0]
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)  # with or without LSE, the same bits
+
+
 def test_matches_forward_flash2_when_plain(cuda):
     q, k, v = (t.to(cuda) for t in orc.make_qkv(2, 4, 512, 64, seed=4))
     for causal in (False, True):
@@ -72,7 +88,7 @@ def test_out_buffer_and_errors(cuda):
 
 
 @pytest.mark.parametrize("B,H,N,causal", [(2, 8, 1024, False), (2, 8, 1024, True), (4, 40, 1000, True),
-                                          (1, 3, 200, False)])
+                                          (1, 3, 200, False), (2, 80, 1000, False)])
 def test_bnhd_layout_equals_bhnd(cuda, B, H, N, causal):
     # [B, N, H, D] (the flash_attn package's layout) through 4-D tensor maps:
     # the same arithmetic as [B, H, N, D], so the bits must agree

@@ -123,6 +123,11 @@ def test_large_logits_rescale_path(cuda):
     # grows by more than 2^8 often, exercising the conditional O rescale
     _run(cuda, 1, 4, 1024, False, seed=3, sm_scale=1.0)
     _run(cuda, 1, 4, 1024, True, seed=4, sm_scale=1.0)
+    # the same over >= 148 full tile pairs (persistent launch: units split
+    # between CTAs are merged from parts with different row maxima); inputs
+    # scaled so |O| < 4, where one fp16 ulp of the output stays below the
+    # absolute tolerance
+    _run(cuda, 1, 150, 512, False, seed=5, sm_scale=2.0, input_scale=0.7)
 
 
 @pytest.mark.parametrize("causal", [False, True])
