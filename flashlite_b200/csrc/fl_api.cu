@@ -160,7 +160,7 @@ int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float
   if (Nq > (1LL << 30) || Nk > (1LL << 30) || B * H > (1LL << 30))
     return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
   if (q_offset < 0 || kv_offset < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative offset");
-  if (D != 64) return fail(FL_ERR_UNSUPPORTED, "FlashLite WMMA kernel currently requires head_dim == 64");
+  if (D != 64 && D != 128) return fail(FL_ERR_UNSUPPORTED, "forward_flash2_ex requires head_dim 64 or 128");
   if (B == 0 || H == 0 || Nq == 0) return FL_OK;
   if (Nk == 0) return fail(FL_ERR_INVALID_ARGUMENT, "empty key sequence");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
@@ -172,7 +172,8 @@ int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
   cudaError_t e = fl::launch_flash2(q, k, v, o, nullptr, lse, B, H, Nq, Nk, q_offset, kv_offset,
                                     scale_log2, is_causal != 0, false, false,
-                                    layout == FL_LAYOUT_BNHD, static_cast<cudaStream_t>(stream));
+                                    layout == FL_LAYOUT_BNHD, static_cast<cudaStream_t>(stream),
+                                    static_cast<int>(D));
   if (e != cudaSuccess) return cuda_fail(e, "flash2 launch");
   return FL_OK;
 }
@@ -199,7 +200,7 @@ int fl_flash2_fwd_block(const void* q, const void* k, const void* v, float* o_ac
                         void* stream) {
   if (!q || !k || !v || !o_acc || !lse) return fail(FL_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (BH < 0 || Nq < 0 || Nk < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative size");
-  if (D != 64) return fail(FL_ERR_UNSUPPORTED, "block kernel requires head_dim == 64");
+  if (D != 64 && D != 128) return fail(FL_ERR_UNSUPPORTED, "block kernel requires head_dim 64 or 128");
   if (Nq > (1LL << 30) || Nk > (1LL << 30) || BH > (1LL << 30))
     return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
   if (q_offset < 0 || kv_offset < 0) return fail(FL_ERR_INVALID_ARGUMENT, "negative offset");
@@ -214,7 +215,7 @@ int fl_flash2_fwd_block(const void* q, const void* k, const void* v, float* o_ac
   const float scale_log2 = static_cast<float>(scale * 1.44269504088896340736);
   cudaError_t e = fl::launch_flash2(q, k, v, nullptr, o_acc, lse, 1, BH, Nq, Nk, q_offset,
                                     kv_offset, scale_log2, is_causal != 0, true, first != 0, false,
-                                    static_cast<cudaStream_t>(stream));
+                                    static_cast<cudaStream_t>(stream), static_cast<int>(D));
   if (e != cudaSuccess) return cuda_fail(e, "flash2 block launch");
   return FL_OK;
 }

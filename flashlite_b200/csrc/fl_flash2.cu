@@ -52,18 +52,56 @@ namespace fl {
 namespace {
 
 constexpr int kBM = 128;       // query rows per tile (UMMA M)
-constexpr int kBN = 128;       // keys per KV tile (UMMA N of S = Q K^T)
-constexpr int kD = 64;         // head dimension
-constexpr int kStagesK = 4;    // K ring depth
-constexpr int kStagesV = 4;    // V ring depth
 constexpr int kThreads = 384;  // 3 warpgroups
-constexpr int kTileBytes = kBM * kD * 2;  // 16 KB, one 128x64 fp16 tile
-
 // Tensor Memory columns (512 allocated: the CTA owns the whole SM's TMEM).
 constexpr uint32_t kTmemCols = 512;
-__host__ __device__ constexpr uint32_t col_s(int i) { return i ? 128u : 0u; }   // S, 128 fp32 cols
-__host__ __device__ constexpr uint32_t col_o(int i) { return i ? 320u : 256u; } // O, 64 fp32 cols
-__host__ __device__ constexpr uint32_t col_p(int i) { return i ? 448u : 384u; } // P, 128 fp16 = 64 cols
+
+// Per-head-dimension shape. Every shared-memory tile is made of 64-column
+// (128-byte) swizzle atoms: a D = 128 row is two atoms side by side, each
+// half of a tile stored as its own [rows x 64] block, loaded and stored by
+// its own TMA copy.
+//   D = 64:  128-key KV tiles; TMEM S 2 x 128 | O 2 x 64  | P 2 x 64 columns.
+//   D = 128:  64-key KV tiles (a K or V tile is still 16 KB and a KV step
+//            the same tensor-core work as at D = 64, with half the
+//            exponentials); TMEM S 2 x 64 | O 2 x 128 | P 2 x 32 columns.
+template <int HD>
+struct Cfg {
+  static_assert(HD == 64 || HD == 128, "head dimension 64 or 128");
+  static constexpr int kD = HD;
+  static constexpr int kBN = HD == 64 ? 128 : 64;      // keys per KV tile (UMMA N of S)
+  static constexpr int kHalves = HD / 64;              // 64-column atoms per row
+  static constexpr int kStagesK = 4;                   // K ring depth
+  static constexpr int kStagesV = 4;                   // V ring depth
+  static constexpr int kQTileBytes = kBM * HD * 2;     // 16 / 32 KB
+  static constexpr int kKVTileBytes = kBN * HD * 2;    // 16 KB
+  // Shared-memory map (offsets from a 1024-byte aligned base).
+  static constexpr int kSmemQ = 0;                                        // 2 tiles
+  static constexpr int kSmemK = kSmemQ + 2 * kQTileBytes;                 // kStagesK tiles
+  static constexpr int kSmemV = kSmemK + kStagesK * kKVTileBytes;         // kStagesV tiles
+  static constexpr int kSmemBar = kSmemV + kStagesV * kKVTileBytes;       // mbarriers
+  // q | k full/empty | v full/empty | s_full, s_free, p_full, pv_done (x2) | drain | stagger
+  static constexpr int kNumBars = 1 + 2 * kStagesK + 2 * kStagesV + 4 * 2 + 2;
+  static constexpr int kSmemMisc = kSmemBar + kNumBars * 8;  // tmem base, abort flag
+  static constexpr int kSmemBytes = kSmemMisc + 16;
+  static constexpr int kSmemAlloc = kSmemBytes + 1024;       // alignment slack
+  // Register split between warpgroup 0 (producers, MMA) and the two softmax
+  // warpgroups; 128 * producer + 256 * softmax <= 384 * 168, the launch total.
+#ifndef FL_D128_REGS_SOFTMAX
+#define FL_D128_REGS_SOFTMAX 216
+#endif
+#ifndef FL_D128_REGS_PRODUCER
+#define FL_D128_REGS_PRODUCER 56
+#endif
+  static constexpr int kRegsProducer = HD == 64 ? 64 : FL_D128_REGS_PRODUCER;
+  static constexpr int kRegsSoftmax = HD == 64 ? 216 : FL_D128_REGS_SOFTMAX;
+  static_assert(128 * kRegsProducer + 256 * kRegsSoftmax <= 384 * 168, "register split");
+  // TMEM columns: S (fp32, kBN), O (fp32, kD), P (fp16 pairs, kBN / 2).
+  __host__ __device__ static constexpr uint32_t col_s(int i) { return i ? kBN : 0u; }
+  __host__ __device__ static constexpr uint32_t col_o(int i) { return 2 * kBN + (i ? kD : 0); }
+  __host__ __device__ static constexpr uint32_t col_p(int i) { return 384u + (i ? kBN / 2 : 0); }
+};
+static_assert(Cfg<64>::col_o(1) + 64 <= 384 && Cfg<128>::col_o(1) + 128 <= 384, "O below P");
+static_assert(Cfg<64>::kSmemAlloc <= 227 * 1024 && Cfg<128>::kSmemAlloc <= 227 * 1024, "smem");
 
 // A row maximum may exceed the reference maximum by up to this much (log2
 // units) before O and l are rescaled: p <= 2^8 stays exact enough in fp16.
@@ -76,8 +114,11 @@ constexpr float kRescaleThreshold = 8.0f;
 #define FL_POLY_PAIRS 0x11
 #endif
 constexpr unsigned kPolyPairs = FL_POLY_PAIRS;
-constexpr int kPolyCols = 16 * __builtin_popcount(kPolyPairs & 0xffu);  // per 128-col row
-static_assert(kPolyCols >= 8 && kPolyCols <= 120, "both exp methods must get columns");
+// FMA-pipe columns of a row of `cols` scores (pattern repeats every 16 columns).
+__host__ __device__ constexpr int poly_cols(int cols) {
+  return cols / 8 * __builtin_popcount(kPolyPairs & 0xffu);
+}
+static_assert(poly_cols(64) >= 8 && poly_cols(64) <= 56, "both exp methods must get columns");
 
 // Maximum of N values in four independent chains of 3-input max.
 template <int N>
@@ -98,26 +139,15 @@ __device__ __forceinline__ float max_chains4(const float* v) {
   return fmax3(fmaxf(part[0], part[1]), part[2], part[3]);
 }
 
-// Shared-memory map (offsets from a 1024-byte aligned base).
-constexpr int kSmemQ = 0;                                  // 2 tiles
-constexpr int kSmemK = kSmemQ + 2 * kTileBytes;            // kStagesK tiles
-constexpr int kSmemV = kSmemK + kStagesK * kTileBytes;     // kStagesV tiles
-constexpr int kSmemBar = kSmemV + kStagesV * kTileBytes;   // mbarriers
-// q | k full/empty | v full/empty | s_full, s_free, p_full, pv_done (x2) | drain | stagger
-constexpr int kNumBars = 1 + 2 * kStagesK + 2 * kStagesV + 4 * 2 + 2;
-constexpr int kSmemMisc = kSmemBar + kNumBars * 8;         // tmem base, abort flag
-constexpr int kSmemBytes = kSmemMisc + 16;
-constexpr int kSmemAlloc = kSmemBytes + 1024;              // alignment slack
-
 struct Flash2Params {
-  // 4-D maps {64, rows, H, B} with box {64, 128, 1, 1}, SW128; the strides
-  // give the [B,H,N,D] or [B,N,H,D] layout, the kernel's coordinates are the
-  // same for both: (0, row, h, b).
-  CUtensorMap tm_q;  // {64, Nq, H, B} fp16
-  CUtensorMap tm_k;  // {64, Nk, H, B}
-  CUtensorMap tm_v;  // {64, Nk, H, B}
-  CUtensorMap tm_o;  // {64, Nq, H, B} (unused in merge mode)
-  float* o_acc;      // merge mode: [BH, Nq, 64] fp32
+  // 4-D maps {D, rows, H, B} with box {64, tile rows, 1, 1}, SW128; the
+  // strides give the [B,H,N,D] or [B,N,H,D] layout, the kernel's coordinates
+  // are the same for both: (64 * half, row, h, b).
+  CUtensorMap tm_q;  // {D, Nq, H, B} fp16, box rows 128
+  CUtensorMap tm_k;  // {D, Nk, H, B}, box rows = KV tile
+  CUtensorMap tm_v;  // {D, Nk, H, B}, box rows = KV tile
+  CUtensorMap tm_o;  // {D, Nq, H, B}, box rows 128 (unused in merge mode)
+  float* o_acc;      // merge mode: [BH, Nq, D] fp32
   float* lse;        // merge mode: [BH, Nq] fp32 (natural log)
   unsigned int* err; // device error word
   int nq, nk;        // query / key rows per slice
@@ -132,7 +162,8 @@ struct Flash2Params {
   int first;         // merge mode: overwrite instead of merge
 };
 
-// Number of KV tiles a query tile starting at row q_start must visit.
+// Number of KV tiles (of kBN keys) a query tile starting at row q_start must visit.
+template <int kBN>
 __device__ __forceinline__ int kv_tiles_for(const Flash2Params& p, bool causal, int q_start) {
   if (!causal) return p.n_ktiles;
   // last visible key position for the tile's last row
@@ -174,19 +205,24 @@ __device__ long long fl_trace_buf[kTraceEvents * kTraceIters];
 #endif
 
 // TMA producer of one ring (K or V): tile t goes to stage t % kStages once
-// the consumer released that stage. Returns the number of tiles issued.
-template <int kStages>
+// the consumer released that stage (one copy per 64-column half). Returns
+// the number of tiles issued.
+template <int HD, int kStages>
 __device__ __forceinline__ int produce_ring(const CUtensorMap* tm, uint32_t s_ring, uint32_t bar_full0,
                                             uint32_t bar_empty0, int n_tiles, int h, int b, int lane,
                                             volatile int* abort_flag, unsigned int* err) {
+  using C = Cfg<HD>;
   int issued = 0;
   for (int t = 0; t < n_tiles; ++t) {
     const int st = t % kStages;
     const uint32_t ph = (t / kStages) & 1;
     if (!warp_wait(bar_empty0 + 8u * st, ph ^ 1, abort_flag, err)) break;
     if (lane == 0) {
-      mbar_arrive_expect_tx(bar_full0 + 8u * st, kTileBytes);
-      tma_load_4d(s_ring + st * kTileBytes, tm, bar_full0 + 8u * st, 0, t * kBN, h, b);
+      mbar_arrive_expect_tx(bar_full0 + 8u * st, C::kKVTileBytes);
+#pragma unroll
+      for (int hh = 0; hh < C::kHalves; ++hh)
+        tma_load_4d(s_ring + st * C::kKVTileBytes + hh * (C::kBN * 128), tm, bar_full0 + 8u * st,
+                    64 * hh, t * C::kBN, h, b);
     }
     __syncwarp();
     issued = t + 1;
@@ -200,16 +236,27 @@ __device__ __forceinline__ void drain_ring(uint32_t bar_full0, int issued) {
     mbar_wait_quiet(bar_full0 + 8u * (t % kStages), (t / kStages) & 1);
 }
 
-template <bool kCausal, bool kMerge>
+template <int HD, bool kCausal, bool kMerge>
 __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_constant__ Flash2Params p) {
+  using C = Cfg<HD>;
+  constexpr int kD = C::kD;
+  constexpr int kBN = C::kBN;
+  constexpr int kStagesK = C::kStagesK;
+  constexpr int kStagesV = C::kStagesV;
+  constexpr int kQTileBytes = C::kQTileBytes;
+  constexpr int kSmemQ = C::kSmemQ;
+  constexpr int kSmemMisc = C::kSmemMisc;
+  constexpr auto col_s = C::col_s;
+  constexpr auto col_o = C::col_o;
+  constexpr auto col_p = C::col_p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t s_q[2] = {sbase + kSmemQ, sbase + kSmemQ + kTileBytes};
-  const uint32_t s_k0 = sbase + kSmemK;
-  const uint32_t s_v0 = sbase + kSmemV;
-  const uint32_t bar_q = sbase + kSmemBar;
+  const uint32_t s_q[2] = {sbase + kSmemQ, sbase + kSmemQ + kQTileBytes};
+  const uint32_t s_k0 = sbase + C::kSmemK;
+  const uint32_t s_v0 = sbase + C::kSmemV;
+  const uint32_t bar_q = sbase + C::kSmemBar;
   const uint32_t bar_kfull0 = bar_q + 8;
   const uint32_t bar_kempty0 = bar_kfull0 + 8 * kStagesK;
   const uint32_t bar_vfull0 = bar_kempty0 + 8 * kStagesK;
@@ -243,8 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   }
   const int qt0 = cta_m * p.tiles_per_cta;
   const bool has_q1 = (p.tiles_per_cta == 2) && (qt0 + 1 < p.n_qtiles);
-  const int nkv0 = kv_tiles_for(p, kCausal, qt0 * kBM);
-  const int nkv1 = has_q1 ? kv_tiles_for(p, kCausal, (qt0 + 1) * kBM) : 0;
+  const int nkv0 = kv_tiles_for<kBN>(p, kCausal, qt0 * kBM);
+  const int nkv1 = has_q1 ? kv_tiles_for<kBN>(p, kCausal, (qt0 + 1) * kBM) : 0;
   const int nkv = nkv0 > nkv1 ? nkv0 : nkv1;
 
   // ---- setup ----
@@ -281,20 +328,26 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   // Register split: warpgroup 0 (K producer, MMA, V producer, idle) gives
   // registers to the softmax warpgroups. Each role's code sits inside the
   // branch of its own setmaxnreg so the compiler allocates it against that
-  // budget (128*64 + 256*216 <= 384*168, the launch total).
+  // budget (Cfg::kRegsProducer / kRegsSoftmax).
   if (warp < 4) {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::kRegsProducer));
   if (warp == 0) {
     // ======================= Q + K producer =======================
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_k);
-      mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kTileBytes);
-      tma_load_4d(s_q[0], &p.tm_q, bar_q, 0, qt0 * kBM, bh % p.nh, bh / p.nh);
-      if (has_q1) tma_load_4d(s_q[1], &p.tm_q, bar_q, 0, (qt0 + 1) * kBM, bh % p.nh, bh / p.nh);
+      mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kQTileBytes);
+#pragma unroll
+      for (int hh = 0; hh < C::kHalves; ++hh) {
+        tma_load_4d(s_q[0] + hh * (kBM * 128), &p.tm_q, bar_q, 64 * hh, qt0 * kBM, bh % p.nh,
+                    bh / p.nh);
+        if (has_q1)
+          tma_load_4d(s_q[1] + hh * (kBM * 128), &p.tm_q, bar_q, 64 * hh, (qt0 + 1) * kBM,
+                      bh % p.nh, bh / p.nh);
+      }
     }
     __syncwarp();
-    const int issued = produce_ring<kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv,
+    const int issued = produce_ring<HD, kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv,
                                               bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) {
       // Drain: let every copy this CTA started land before shared memory is released.
@@ -304,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   } else if (warp == 2) {
     // ======================= V producer =======================
     if (lane == 0) tma_prefetch_desc(&p.tm_v);
-    const int issued = produce_ring<kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv,
+    const int issued = produce_ring<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv,
                                               bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
   } else if (warp == 1) {
@@ -315,13 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     // keeps every MMA operand in uniform registers; one elected lane issues.
     // (Operands built in lane-0-only code cost ~100 cycles per tcgen05.mma.)
     // Descriptors advance by constants: +32 B per K step inside a 128B-swizzled
-    // K-major row (encoded +2), +2048 B per 16 keys of MN-major V (encoded +128).
+    // K-major row (encoded +2), to the next 64-column half block after four
+    // K steps (D = 128), +2048 B per 16 keys of MN-major V (encoded +128); V's
+    // two 64-column halves (D = 128) are one leading-byte-offset apart.
     const uint32_t tm = __shfl_sync(0xffffffffu, tmem, 0);
     const uint64_t dq0 = make_sdesc_sw128(s_q[0], 16, 1024);
     const uint64_t dq1 = make_sdesc_sw128(s_q[1], 16, 1024);
     const uint64_t dk0 = make_sdesc_sw128(s_k0, 16, 1024);
-    const uint64_t dv0 = make_sdesc_sw128(s_v0, 8192, 1024);
-    constexpr uint64_t kStageEnc = kTileBytes >> 4;  // one stage in descriptor units
+    const uint64_t dv0 = make_sdesc_sw128(s_v0, HD == 64 ? 8192 : kBN * 128, 1024);
+    constexpr uint64_t kStageEnc = C::kKVTileBytes >> 4;  // one stage in descriptor units
+    constexpr uint64_t kQHalfEnc = (kBM * 128) >> 4;      // Q half block
+    constexpr uint64_t kKHalfEnc = (kBN * 128) >> 4;      // K half block
     auto issue_s = [&](int i, int st) {
       const uint64_t a = i ? dq1 : dq0;
       const uint64_t b = dk0 + static_cast<uint64_t>(st) * kStageEnc;
@@ -329,7 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          umma_f16_ss(d, a + 2 * kk, b + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+          umma_f16_ss(d, a + 2 * (kk & 3) + (kk >> 2) * kQHalfEnc, b + 2 * (kk & 3) + (kk >> 2) * kKHalfEnc,
+                      idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(bar_s(i));
       }
       __syncwarp();
@@ -417,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   }
   // warp 3 has no role in this design.
   } else {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 216;\n");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::kRegsSoftmax));
   {
     // ======================= softmax warpgroups =======================
     const int i = (warp - 4) >> 2;               // query tile handled: 0 or 1
@@ -446,20 +504,24 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (!warp_wait(bar_s(i), j & 1, abort_flag, p.err)) { ok = false; break; }
       if (t == 0) FL_TRACE_EV(0 + 4 * i, j);
       tc_fence_after();
-      uint32_t sr[128];
-      tmem_ld128_wait(tS, sr);
+      uint32_t sr[kBN];
+      if constexpr (kBN == 128) {
+        tmem_ld128_wait(tS, sr);
+      } else {
+        tmem_ld64_wait(tS, sr);
+      }
       // S_i is in registers: let the tensor core overwrite it with S_{i,j+1}.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sfree(i));
       if (t == 0) FL_TRACE_EV(1 + 4 * i, j);
-      float s[128];
+      float s[kBN];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
+      for (int c = 0; c < kBN; ++c) s[c] = __uint_as_float(sr[c]);
       float scl = sc;
       if (prescale) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] *= sc;
+        for (int c = 0; c < kBN; ++c) s[c] *= sc;
         scl = 1.0f;
       }
       const int k_start = j * kBN;
@@ -472,18 +534,18 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (lim < kBN) {
         const int limit = lim < 0 ? 0 : static_cast<int>(lim);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
+        for (int c = 0; c < kBN; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
       }
       // Row maximum, kept separately over the columns exponentiated on the
       // FMA pipe (mxp) and on the MUFU (mxm): 3-input max chains, several
       // independent per class (no 127-long dependency chain).
       float mxp, mxm;
       {
-        constexpr int kNP = kPolyCols, kNM = 128 - kNP;  // per row
+        constexpr int kNP = poly_cols(kBN), kNM = kBN - kNP;  // per row
         float vp[kNP], vm[kNM];
         int np = 0, nm = 0;
 #pragma unroll
-        for (int c = 0; c < 128; c += 2) {
+        for (int c = 0; c < kBN; c += 2) {
           const int e = (c >> 1) & 15;
           if ((kPolyPairs >> (e & 7)) & 1) {
             vp[np++] = s[c];
@@ -515,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         if (__any_sync(0xffffffffu, need)) {
           uint32_t o[32];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < kD / 32; ++h) {
             tmem_ld32_wait(tO + h * 32, o);
 #pragma unroll
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
@@ -532,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       float2 lsum[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < kBN / 32; ++q) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -547,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
           pk[e] = pack_f16x2(pp.x, pp.y);
         }
         tmem_st16(tP + q * 16, pk);
-        if (q == 1 && !stagger_sent) {
+        if (q == kBN / 64 - 1 && !stagger_sent) {  // half-way through the tile
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_stagger);
           stagger_sent = true;
@@ -582,16 +644,16 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     // ---- epilogue ----
     if (active && my_nkv > 0 && ok) ok = warp_wait(bar_pv(i), (my_nkv - 1) & 1, abort_flag, p.err);
     const bool do_out = active && my_nkv > 0 && ok;
-    uint32_t o[64];
+    uint32_t o[kD];
     if (do_out) {
       tc_fence_after();
       uint32_t tmp[32];
-      tmem_ld32_wait(tO, tmp);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = tmp[c];
-      tmem_ld32_wait(tO + 32, tmp);
+      for (int h = 0; h < kD / 32; ++h) {
+        tmem_ld32_wait(tO + h * 32, tmp);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[32 + c] = tmp[c];
+        for (int c = 0; c < 32; ++c) o[32 * h + c] = tmp[c];
+      }
     }
     const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
     if (!kMerge) {
@@ -603,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         // (with no KV step nothing else waited for it).
         warp_wait(bar_q, 0, abort_flag, p.err);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) o[c] = 0u;
+        for (int c = 0; c < kD; ++c) o[c] = 0u;
       }
       if (p.lse != nullptr && write && q_start + t < p.nq)
         p.lse[static_cast<long long>(bh) * p.nq + q_start + t] =
@@ -611,22 +673,24 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       if (write) {
         // Stage the fp16 tile in the (now unused) Q buffer with the 128B
         // swizzle the TMA store expects: 16-byte chunk c of row t goes to
-        // chunk position c ^ (t % 8).
-        uint8_t* row = smem + kSmemQ + i * kTileBytes + t * 128;
+        // chunk position c % 8 ^ (t % 8) of half block c / 8.
+        uint8_t* row = smem + kSmemQ + i * kQTileBytes + t * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < kD / 8; ++c) {
           uint4 v;
           v.x = pack_f16x2(__uint_as_float(o[8 * c + 0]) * inv_l, __uint_as_float(o[8 * c + 1]) * inv_l);
           v.y = pack_f16x2(__uint_as_float(o[8 * c + 2]) * inv_l, __uint_as_float(o[8 * c + 3]) * inv_l);
           v.z = pack_f16x2(__uint_as_float(o[8 * c + 4]) * inv_l, __uint_as_float(o[8 * c + 5]) * inv_l);
           v.w = pack_f16x2(__uint_as_float(o[8 * c + 6]) * inv_l, __uint_as_float(o[8 * c + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(row + ((c ^ (t & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(row + (c >> 3) * (kBM * 128) + (((c & 7) ^ (t & 7)) << 4)) = v;
         }
         fence_proxy_async_smem();
       }
       named_bar_sync(1 + i, 128);
       if (write && t == 0 && !*abort_flag) {
-        tma_store_4d(&p.tm_o, s_q[i], 0, q_start, bh % p.nh, bh / p.nh);
+#pragma unroll
+        for (int hh = 0; hh < C::kHalves; ++hh)
+          tma_store_4d(&p.tm_o, s_q[i] + hh * (kBM * 128), 64 * hh, q_start, bh % p.nh, bh / p.nh);
         tma_store_commit();
         tma_store_wait_read0();
       }
@@ -654,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         }
         const float wn = w_new * inv_l;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < kD / 4; ++c) {
           float4 r;
           const float o0 = do_out ? __uint_as_float(o[4 * c + 0]) : 0.0f;
           const float o1 = do_out ? __uint_as_float(o[4 * c + 1]) : 0.0f;
@@ -705,14 +769,15 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// Tensor map {64, rows, H, B} over a [B,H,rows,64] (bnhd = false) or
-// [B,rows,H,64] (bnhd = true) fp16 array, box {64, 128, 1, 1}.
+// Tensor map {D, rows, H, B} over a [B,H,rows,D] (bnhd = false) or
+// [B,rows,H,D] (bnhd = true) fp16 array, box {64, box_rows, 1, 1} (one
+// 128-byte swizzle atom wide: a D = 128 tile is copied as two halves).
 bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H, int64_t B,
-                     bool bnhd) {
+                     bool bnhd, int D, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  const cuuint64_t row_b = kD * 2;  // bytes of one 64-wide fp16 row
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows),
+  const cuuint64_t row_b = static_cast<cuuint64_t>(D) * 2;  // bytes of one fp16 row
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3];
   if (!bnhd) {
@@ -723,7 +788,7 @@ bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H,
     strides[1] = row_b;                                       // next head
   }
   strides[2] = static_cast<cuuint64_t>(rows) * H * row_b;     // next batch entry
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kBM), 1, 1};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -731,9 +796,10 @@ bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H,
   return r == CUDA_SUCCESS;
 }
 
-template <bool kCausal, bool kMerge>
+template <int HD, bool kCausal, bool kMerge>
 cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t stream) {
-  auto kern = flash2_fwd_kernel<kCausal, kMerge>;
+  constexpr int kSmemAlloc = Cfg<HD>::kSmemAlloc;
+  auto kern = flash2_fwd_kernel<HD, kCausal, kMerge>;
   static int configured_mask = 0;  // bit per device (up to 32 devices)
   int dev = 0;
   cudaGetDevice(&dev);
@@ -751,16 +817,18 @@ cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t strea
 cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
                           float* lse, int64_t B, int64_t H, int64_t Nq, int64_t Nk,
                           int64_t q_offset, int64_t kv_offset, float scale_log2, bool causal,
-                          bool merge, bool first, bool bnhd, cudaStream_t stream) {
+                          bool merge, bool first, bool bnhd, cudaStream_t stream, int head_dim) {
+  if (head_dim != 64 && head_dim != 128) return cudaErrorInvalidValue;
   Flash2Params prm;
   const int64_t BH = B * H;
-  if (!encode_rows_map(&prm.tm_q, q, Nq, H, B, bnhd) ||
-      !encode_rows_map(&prm.tm_k, k, Nk, H, B, bnhd) ||
-      !encode_rows_map(&prm.tm_v, v, Nk, H, B, bnhd)) {
+  const int kv_rows = head_dim == 64 ? Cfg<64>::kBN : Cfg<128>::kBN;  // keys per KV tile
+  if (!encode_rows_map(&prm.tm_q, q, Nq, H, B, bnhd, head_dim, kBM) ||
+      !encode_rows_map(&prm.tm_k, k, Nk, H, B, bnhd, head_dim, kv_rows) ||
+      !encode_rows_map(&prm.tm_v, v, Nk, H, B, bnhd, head_dim, kv_rows)) {
     return cudaErrorInvalidValue;
   }
   if (!merge) {
-    if (!encode_rows_map(&prm.tm_o, o_f16, Nq, H, B, bnhd)) return cudaErrorInvalidValue;
+    if (!encode_rows_map(&prm.tm_o, o_f16, Nq, H, B, bnhd, head_dim, kBM)) return cudaErrorInvalidValue;
   } else {
     prm.tm_o = prm.tm_q;
   }
@@ -772,7 +840,7 @@ cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f
   prm.nk = static_cast<int>(Nk);
   prm.bh = static_cast<int>(BH);
   prm.n_qtiles = static_cast<int>((Nq + kBM - 1) / kBM);
-  prm.n_ktiles = static_cast<int>((Nk + kBN - 1) / kBN);
+  prm.n_ktiles = static_cast<int>((Nk + kv_rows - 1) / kv_rows);
   const int64_t pairs = (prm.n_qtiles + 1) / 2;
   // Two query tiles per CTA keep the tensor core busy while one tile is in
   // softmax; fall back to one tile per CTA when that would leave SMs idle.
@@ -784,12 +852,21 @@ cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f
   prm.first = first ? 1 : 0;
   const int64_t grid = static_cast<int64_t>(prm.n_cta_m) * BH;
   if (grid <= 0 || grid > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  if (merge) {
-    return causal ? launch_variant<true, true>(prm, static_cast<int>(grid), stream)
-                  : launch_variant<false, true>(prm, static_cast<int>(grid), stream);
+  const int g = static_cast<int>(grid);
+  if (head_dim == 128) {
+    if (merge) {
+      return causal ? launch_variant<128, true, true>(prm, g, stream)
+                    : launch_variant<128, false, true>(prm, g, stream);
+    }
+    return causal ? launch_variant<128, true, false>(prm, g, stream)
+                  : launch_variant<128, false, false>(prm, g, stream);
   }
-  return causal ? launch_variant<true, false>(prm, static_cast<int>(grid), stream)
-                : launch_variant<false, false>(prm, static_cast<int>(grid), stream);
+  if (merge) {
+    return causal ? launch_variant<64, true, true>(prm, g, stream)
+                  : launch_variant<64, false, true>(prm, g, stream);
+  }
+  return causal ? launch_variant<64, true, false>(prm, g, stream)
+                : launch_variant<64, false, false>(prm, g, stream);
 }
 
 }  // namespace fl

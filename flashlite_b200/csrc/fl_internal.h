@@ -22,11 +22,13 @@ int sm_count();
 bool prepare_current_device();
 
 // Launchers. All sizes validated by the caller; return 0 or a cudaError_t.
-// q/k/v/o are [B,H,N,64] fp16, or [B,N,H,64] with bnhd (non-merge only).
+// q/k/v/o are [B,H,N,D] fp16, or [B,N,H,D] with bnhd (non-merge only);
+// head_dim D is 64 or 128.
 cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f16, float* o_acc,
                           float* lse, int64_t B, int64_t H, int64_t Nq, int64_t Nk,
                           int64_t q_offset, int64_t kv_offset, float scale_log2, bool causal,
-                          bool merge, bool first, bool bnhd, cudaStream_t stream);
+                          bool merge, bool first, bool bnhd, cudaStream_t stream,
+                          int head_dim = 64);
 
 cudaError_t launch_naive(const void* q, const void* k, const void* v, void* o, int64_t BH,
                          int64_t N, int64_t D, float sm_scale, bool causal, cudaStream_t stream);

@@ -347,6 +347,24 @@ __device__ __forceinline__ void tmem_wait_ld_dep(uint32_t (&r)[32]) {
       : "memory");
 }
 
+// Two x32 loads (64 consecutive columns) followed by a single wait.
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t (&r)[64]) {
+#define FL_R8(b) "=r"(r[b]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), \
+                 "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : FL_R8(0), FL_R8(8), FL_R8(16), FL_R8(24), FL_R8(32), FL_R8(40), FL_R8(48), FL_R8(56)
+      : "r"(taddr), "r"(taddr + 32u)
+      : "memory");
+#undef FL_R8
+}
+
 // Four x32 loads (128 consecutive columns) followed by a single wait.
 __device__ __forceinline__ void tmem_ld128_wait(uint32_t taddr, uint32_t (&r)[128]) {
 #define FL_R8(b) "=r"(r[b]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), \

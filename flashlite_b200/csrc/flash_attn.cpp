@@ -123,7 +123,7 @@ std::vector<torch::Tensor> forward_flash2_ex(torch::Tensor q, torch::Tensor k, t
               bnhd ? "Key dimensions must match Query dimensions [B, N_k, H, D]"
                    : "Key dimensions must match Query dimensions [B, H, N_k, D]");
   TORCH_CHECK(v.sizes() == k.sizes(), "Value dimensions must match Key dimensions [B, H, N_k, D]");
-  TORCH_CHECK(D == 64, "FlashLite WMMA kernel currently requires head_dim == 64");
+  TORCH_CHECK(D == 64 || D == 128, "forward_flash2_ex requires head_dim 64 or 128");
   TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
               "All tensors must be on the same CUDA device");
   torch::Tensor out_tensor;

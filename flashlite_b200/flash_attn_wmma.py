@@ -17,10 +17,12 @@ raises ImportError.
 
 Extra entry points (no reference counterpart):
 ``forward_flash2_ex(q, k, v, sm_scale=0.0, is_causal=False, q_offset=0,
-kv_offset=0, out=None, return_lse=False) -> (out, lse)`` takes N_k != N_q
-and global positions (query row i at q_offset + i, key row j at
-kv_offset + j) and can return the per-row log-sum-exp; ``forward_block`` and
-``ring_finalize`` are the ring-attention steps; ``device_error`` reads the
+kv_offset=0, out=None, return_lse=False, layout="bhnd") -> (out, lse)`` takes
+head_dim 64 or 128, N_k != N_q and global positions (query row i at
+q_offset + i, key row j at kv_offset + j), the ``[B, N, H, D]`` layout
+(``layout="bnhd"``), and can return the per-row log-sum-exp;
+``forward_block`` (head_dim 64 or 128) and ``ring_finalize`` are the
+ring-attention steps; ``device_error`` reads the
 error bits kernels raise when a bounded wait gives up.
 """
 from __future__ import annotations

@@ -54,13 +54,14 @@ enum fl_layout {
  * optional log-sum-exp output and a choice of layout; no reference
  * counterpart (the reference's forward_flash2 assumes N_k == N_q without
  * checking it, csrc/kernel_flash2.cu:749-755, and takes [B, H, N, D] only).
- * q, o: [B, H, Nq, 64] (or [B, Nq, H, 64] with FL_LAYOUT_BNHD) fp16; k, v:
- * [B, H, Nk, 64] (or [B, Nk, H, 64]) fp16. Query row i sits at position
- * q_offset + i and key row j at kv_offset + j; with is_causal a query sees
- * the keys at positions <= its own. lse (may be NULL): [B, H, Nq] fp32 in
- * either layout, natural-log log-sum-exp of the scaled scores of each row
- * (-inf for a row without visible keys, whose output is zero).
- * sm_scale == 0 means 1/sqrt(64).
+ * q, o: [B, H, Nq, D] (or [B, Nq, H, D] with FL_LAYOUT_BNHD) fp16; k, v:
+ * [B, H, Nk, D] (or [B, Nk, H, D]) fp16; D is 64 or 128 (the reference
+ * takes 64 only, csrc/kernel_flash2.cu:756-757). Query row i sits at
+ * position q_offset + i and key row j at kv_offset + j; with is_causal a
+ * query sees the keys at positions <= its own. lse (may be NULL): [B, H, Nq]
+ * fp32 in either layout, natural-log log-sum-exp of the scaled scores of
+ * each row (-inf for a row without visible keys, whose output is zero).
+ * sm_scale == 0 means 1/sqrt(D).
  */
 int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
                      int64_t H, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
@@ -76,10 +77,11 @@ int fl_naive_fwd(const void* q, const void* k, const void* v, void* o, int64_t B
 /*
  * One block step of sequence-sharded (ring) attention; no reference
  * counterpart (the reference is single-GPU). Attends the query block q
- * [BH, Nq, 64] (global positions q_offset..q_offset+Nq-1) to the key/value
- * block k, v [BH, Nk, 64] (positions kv_offset..), causal by global position
- * when is_causal != 0, and merges the result into the running state:
- *   o_acc  [BH, Nq, 64] fp32, normalised partial output
+ * [BH, Nq, D] (global positions q_offset..q_offset+Nq-1, D = 64 or 128) to
+ * the key/value block k, v [BH, Nk, D] (positions kv_offset..), causal by
+ * global position when is_causal != 0, and merges the result into the
+ * running state:
+ *   o_acc  [BH, Nq, D]  fp32, normalised partial output
  *   lse    [BH, Nq]     fp32, natural-log sum-exp of the scaled scores
  * If `first` != 0 the running state is overwritten instead of merged.
  * Rows with no visible key keep (o_acc, lse) = (0, -inf) when `first`.
