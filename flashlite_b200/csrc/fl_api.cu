@@ -61,7 +61,12 @@ unsigned int* device_error_word() {
   return (dev >= 0 && dev < kMaxDevices) ? g_err_ptr[dev] : nullptr;
 }
 
-bool prepare_current_device() { return init_device(current_device()); }
+bool prepare_current_device() {
+  const int dev = current_device();
+  // binds the primary context to this thread (see check_device)
+  if (dev < 0 || cudaSetDevice(dev) != cudaSuccess) return false;
+  return init_device(dev);
+}
 
 int sm_count() {
   const int dev = current_device();
@@ -99,6 +104,11 @@ int check_common(const void* q, const void* k, const void* v, const void* o, int
 int check_device() {
   const int dev = fl::current_device();
   if (dev < 0) return fail(FL_ERR_NO_DEVICE, "no CUDA device");
+  // Bind the device's primary context to this thread: tensor maps are encoded
+  // through the driver API before the first runtime launch, and a thread
+  // that has only queried the device (an autograd worker, say) has no
+  // current context yet.
+  if (cudaSetDevice(dev) != cudaSuccess) return fail(FL_ERR_NO_DEVICE, "cannot bind the CUDA device");
   if (!fl::init_device(dev)) return fail(FL_ERR_CUDA, "device initialisation failed");
   int major = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
@@ -230,6 +240,41 @@ int fl_ring_finalize(const float* o_acc, void* o, int64_t n_elems, void* stream)
   if (st != FL_OK) return st;
   cudaError_t e = fl::launch_ring_finalize(o_acc, o, n_elems, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
+  return FL_OK;
+}
+
+size_t fl_flash2_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D) {
+  if (B <= 0 || H <= 0 || N <= 0 || D != 64 || N > (1LL << 30) || B * H > (1LL << 30)) return 0;
+  return fl::flash2_bwd_workspace_bytes(B * H, N);
+}
+
+int fl_flash2_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                  const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                  size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D,
+                  float sm_scale, int is_causal, void* stream) {
+  int st = check_common(q, k, v, o, B, H, N, D);
+  if (st != FL_OK) return st;
+  if (!dout || !lse || !dq || !dk || !dv) return fail(FL_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (D != 64) return fail(FL_ERR_UNSUPPORTED, "backward_flash2 requires head_dim == 64");
+  if (B == 0 || H == 0 || N == 0) return FL_OK;
+  if (B * H > (1LL << 30)) return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
+  const size_t need = fl::flash2_bwd_workspace_bytes(B * H, N);
+  if (!workspace || workspace_bytes < need)
+    return fail(FL_ERR_INVALID_ARGUMENT,
+                "workspace too small: " + std::to_string(need) + " bytes needed (fl_flash2_bwd_workspace_size)");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dout) ||
+      !aligned16(dk) || !aligned16(dv) || !aligned16(workspace) || (reinterpret_cast<uintptr_t>(dq) & 3u) ||
+      (reinterpret_cast<uintptr_t>(lse) & 3u))
+    return fail(FL_ERR_MISALIGNED, "q, k, v, out, dout, dk, dv and workspace must be 16-byte aligned");
+  st = check_device();
+  if (st != FL_OK) return st;
+  double scale = sm_scale;
+  if (scale == 0.0) scale = 1.0f / std::sqrt(static_cast<float>(D));
+  const char* where = "flash2 backward";
+  cudaError_t e = fl::launch_flash2_bwd(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, H, N,
+                                        static_cast<float>(scale), is_causal != 0,
+                                        static_cast<cudaStream_t>(stream), &where);
+  if (e != cudaSuccess) return cuda_fail(e, (std::string("flash2 backward: ") + where).c_str());
   return FL_OK;
 }
 

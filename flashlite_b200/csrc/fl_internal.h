@@ -1,6 +1,7 @@
 // Internal (host-side) declarations shared by the library's translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <string>
@@ -21,6 +22,19 @@ int sm_count();
 // C-ABI entry points do before their first launch); false on failure.
 bool prepare_current_device();
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link dependency); nullptr when unavailable.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn get_encode_fn();
+
+// fp16 tensor map {D, rows, H, B} over [B,H,rows,D] (bnhd = false) or
+// [B,rows,H,D] (bnhd = true), box {64, box_rows, 1, 1}, 128-byte swizzle.
+bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H, int64_t B,
+                     bool bnhd, int D, int box_rows);
+
 // Launchers. All sizes validated by the caller; return 0 or a cudaError_t.
 // q/k/v/o are [B,H,N,D] fp16, or [B,N,H,D] with bnhd (non-merge only);
 // head_dim D is 64 or 128.
@@ -29,6 +43,15 @@ cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f
                           int64_t q_offset, int64_t kv_offset, float scale_log2, bool causal,
                           bool merge, bool first, bool bnhd, cudaStream_t stream,
                           int head_dim = 64);
+
+// FA2 backward (head_dim 64, [B,H,N,64] fp16): dq, dk, dv from q, k, v, the
+// forward output o, its gradient dout and the forward's natural-log LSE
+// [B,H,N] fp32. workspace: flash2_bwd_workspace_bytes(B*H, N) bytes.
+size_t flash2_bwd_workspace_bytes(int64_t BH, int64_t N);
+cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const void* o,
+                              const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                              void* workspace, int64_t B, int64_t H, int64_t N, float sm_scale,
+                              bool causal, cudaStream_t stream, const char** where);
 
 cudaError_t launch_naive(const void* q, const void* k, const void* v, void* o, int64_t BH,
                          int64_t N, int64_t D, float sm_scale, bool causal, cudaStream_t stream);

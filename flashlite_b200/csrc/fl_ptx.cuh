@@ -183,6 +183,26 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src
       : "memory");
 }
 
+// Element-wise add of a shared-memory tile into global memory through the
+// tensor map (fp32 reduce; no multicast).
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* tm, uint32_t src, int x, int y,
+                                                  int z, int w) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both
+// addresses 16-byte aligned), completing on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -197,6 +217,13 @@ __device__ __forceinline__ void tma_store_wait0() {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte shared-memory store at a shared-window address.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
 
 // Named barrier over `nthreads` threads (ids 1..15; id 0 is __syncthreads).
@@ -277,8 +304,9 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 // Instruction descriptor, .kind::f16, fp16 A/B, fp32 accumulator, dense.
 //   bits 4-5 D format (1 = F32), 7-9 A format (0 = F16), 10-12 B format,
 //   15 A major (0 = K), 16 B major (0 = K, 1 = MN), 17-22 N>>3, 24-28 M>>4.
-__host__ __device__ constexpr uint32_t make_idesc_f16_f32(int M, int N, bool b_mn_major) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) |
+__host__ __device__ constexpr uint32_t make_idesc_f16_f32(int M, int N, bool b_mn_major,
+                                                          bool a_mn_major = false) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
          ((b_mn_major ? 1u : 0u) << 16) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 

@@ -194,6 +194,39 @@ int64_t device_error() {
   return static_cast<int64_t>(flags);
 }
 
+// FA2 backward (no reference counterpart): gradients of
+// softmax(sm_scale * q k^T) v given the forward output `out`, its gradient
+// `dout` and the forward's LSE (forward_flash2_ex(..., return_lse=True)).
+// Returns (dq, dk, dv); the fp32 workspace is a torch allocation.
+std::vector<torch::Tensor> backward_flash2(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                           torch::Tensor out, torch::Tensor dout, torch::Tensor lse,
+                                           double sm_scale, bool is_causal) {
+  for (const torch::Tensor* t : {&q, &k, &v, &out, &dout}) {
+    TORCH_CHECK(t->is_cuda(), "All tensors must be on CUDA");
+    TORCH_CHECK(t->is_contiguous(), "All tensors must be contiguous");
+    TORCH_CHECK(t->dtype() == torch::kHalf, "q, k, v, out and dout must be FP16 (Half)");
+    TORCH_CHECK(t->dim() == 4, "Tensors must be 4D [B, H, N, D]");
+    TORCH_CHECK(t->sizes() == q.sizes(), "q, k, v, out and dout must have the same shape [B, H, N, D]");
+    TORCH_CHECK(t->device() == q.device(), "All tensors must be on the same CUDA device");
+  }
+  const int64_t B = q.size(0), H = q.size(1), N = q.size(2), D = q.size(3);
+  TORCH_CHECK(D == 64, "backward_flash2 requires head_dim == 64");
+  TORCH_CHECK(lse.is_cuda() && lse.is_contiguous() && lse.dtype() == torch::kFloat &&
+                  lse.device() == q.device(),
+              "lse must be a contiguous float32 CUDA tensor on q's device");
+  TORCH_CHECK(lse.numel() == B * H * N, "lse must hold B*H*N values [B, H, N]");
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  if (q.numel() == 0) return {dq, dk, dv};
+  const c10::cuda::CUDAGuard guard(q.device());
+  const size_t ws_bytes = fl_flash2_bwd_workspace_size(B, H, N, D);
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(torch::kUInt8));
+  check_status(fl_flash2_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                             lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                             ws.data_ptr(), ws_bytes, B, H, N, D, static_cast<float>(sm_scale),
+                             is_causal ? 1 : 0, stream_of(q)));
+  return {dq, dk, dv};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -215,5 +248,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("is_causal") = true, py::arg("first") = false);
   m.def("ring_finalize", &ring_finalize, "Cast the merged fp32 ring output to fp16",
         py::arg("o_acc"), py::arg("out"));
+  m.def("backward_flash2", &backward_flash2,
+        "FA2 backward (tcgen05, sm_100a); returns (dq, dk, dv)", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("sm_scale") = 0.0,
+        py::arg("is_causal") = false);
   m.def("device_error", &device_error, "Read and clear kernel error flags (synchronises)");
 }

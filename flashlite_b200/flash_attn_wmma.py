@@ -22,7 +22,10 @@ head_dim 64 or 128, N_k != N_q and global positions (query row i at
 q_offset + i, key row j at kv_offset + j), the ``[B, N, H, D]`` layout
 (``layout="bnhd"``), and can return the per-row log-sum-exp;
 ``forward_block`` (head_dim 64 or 128) and ``ring_finalize`` are the
-ring-attention steps; ``device_error`` reads the
+ring-attention steps; ``backward_flash2(q, k, v, out, dout, lse, sm_scale=0.0,
+is_causal=False) -> (dq, dk, dv)`` is the FA2 backward (head_dim 64; ``lse`` from
+``forward_flash2_ex(..., return_lse=True)``, wrapped for autograd by
+``flashlite_b200.attention.flash_attention``); ``device_error`` reads the
 error bits kernels raise when a bounded wait gives up.
 """
 from __future__ import annotations
@@ -30,8 +33,8 @@ from __future__ import annotations
 import torch  # noqa: F401  (loads libtorch/libc10 for the binding)
 
 try:
-    from ._C import (device_error, forward_block, forward_flash2, forward_flash2_ex,
-                     forward_naive, ring_finalize)
+    from ._C import (backward_flash2, device_error, forward_block, forward_flash2,
+                     forward_flash2_ex, forward_naive, ring_finalize)
 except ImportError as exc:  # pragma: no cover - exercised only on unbuilt trees
     raise ImportError(
         "flashlite_b200 native extension is not built; run `python -m flashlite_b200.build` "
@@ -39,4 +42,4 @@ except ImportError as exc:  # pragma: no cover - exercised only on unbuilt trees
     ) from exc
 
 __all__ = ["forward_flash2", "forward_naive", "forward_flash2_ex", "forward_block", "ring_finalize",
-           "device_error"]
+           "backward_flash2", "device_error"]

@@ -16,6 +16,7 @@
 #ifndef FLASHLITE_B200_H_
 #define FLASHLITE_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -66,6 +67,22 @@ enum fl_layout {
 int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
                      int64_t H, int64_t Nq, int64_t Nk, int64_t D, int64_t q_offset,
                      int64_t kv_offset, float sm_scale, int is_causal, int layout, void* stream);
+
+/*
+ * FA2 backward; no reference counterpart (the reference is forward-only).
+ * q, k, v, o, dout, dq, dk, dv: [B, H, N, 64] fp16 (o = the forward output,
+ * dout = dL/do); lse: [B, H, N] fp32, the natural-log log-sum-exp the
+ * forward returns (fl_flash2_fwd_ex with a non-NULL lse). Computes dq, dk,
+ * dv of softmax(sm_scale * q k^T [causal mask]) v; sm_scale == 0 means
+ * 1/sqrt(64). workspace: device memory of at least
+ * fl_flash2_bwd_workspace_size(B, H, N, D) bytes, 16-byte aligned (fp32 dq
+ * accumulator and per-row vectors; nothing is allocated by the call).
+ */
+size_t fl_flash2_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D);
+int fl_flash2_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                  const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                  size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D,
+                  float sm_scale, int is_causal, void* stream);
 
 /*
  * Naive (unfused, fp32 CUDA-core) attention forward, any D in [1, 1024].

@@ -19,6 +19,12 @@ What it restates (thebigblender/FlashLite, paths relative to that repo):
   sums the unrounded fp32 p (:278-294, :339), O * (1/l or 0) (:364-369).
   Used to show the tolerance is met by the reference's own numerics.
 * ``flops``: ``benchmarks/benchmark_throughput.py:23-31``.
+* ``attention_backward_fp32``: gradients of ``attention_fp32`` (no reference
+  counterpart: the reference is forward-only). The standard softmax-attention
+  backward (FlashAttention-2, Dao 2023, Algorithm 2): dV = P^T dO,
+  dP = dO V^T, D_i = rowsum(dO_i * O_i), dS = P * (dP - D),
+  dQ = scale dS K, dK = scale dS^T Q, in fp32. Pinned against
+  ``torch.autograd`` in ``tests/test_oracle.py``.
 
 Pinning: ``tests/test_oracle.py`` checks ``attention_fp32`` against
 ``torch.nn.functional.scaled_dot_product_attention`` (the reference tests'
@@ -82,6 +88,36 @@ def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: 
         s = s.masked_fill(mask, float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.matmul(p, vf)
+
+
+def attention_backward_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, do: torch.Tensor,
+                            sm_scale: float = 0.0, is_causal: bool = False):
+    """fp32 gradients (dq, dk, dv) of attention_fp32 for the output gradient do."""
+    D = q.shape[-1]
+    scale = default_scale(D, sm_scale)
+    qf, kf, vf, dof = (t.detach().to("cpu", torch.float32) for t in (q, k, v, do))
+    s = torch.matmul(qf, kf.transpose(-2, -1)) * scale
+    if is_causal:
+        n, m = s.shape[-2], s.shape[-1]
+        s = s.masked_fill(torch.ones(n, m, dtype=torch.bool).triu(1), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = torch.matmul(p, vf)
+    dv = torch.matmul(p.transpose(-2, -1), dof)
+    dp = torch.matmul(dof, vf.transpose(-2, -1))
+    delta = (dof * o).sum(dim=-1, keepdim=True)
+    ds = p * (dp - delta)
+    dq = torch.matmul(ds, kf) * scale
+    dk = torch.matmul(ds.transpose(-2, -1), qf) * scale
+    return dq, dk, dv
+
+
+def grad_error_metrics(got: torch.Tensor, ref: torch.Tensor) -> tuple[float, float]:
+    """(max-abs error / max |ref|, mean-abs error / mean |ref|) of a gradient."""
+    g = got.detach().to("cpu", torch.float32)
+    r = ref.detach().to("cpu", torch.float32)
+    err = (g - r).abs()
+    return (err.max().item() / max(r.abs().max().item(), 1e-30),
+            err.mean().item() / max(r.abs().mean().item(), 1e-30))
 
 
 def attention_rows_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows,
