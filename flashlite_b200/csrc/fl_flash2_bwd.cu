@@ -11,12 +11,14 @@
 //    the CTA streams every query tile that sees them (causal: from the
 //    diagonal tile on) through a 2-deep TMA ring of (Q, dO, LSE, Delta).
 //  * everything is computed key-major, so TMEM lanes are the CTA's keys:
-//    S^T = K Q^T and dP^T = V dO^T land in TMEM (128 columns each); the
-//    gradient warpgroup (one thread per key) turns them into P^T and dS^T
-//    chunk by chunk (P needs no row reduction: LSE is known), writes both
-//    back into the columns it has already read (fp16 pairs, operand A of the
-//    next MMAs), and writes dS^T to shared memory in the MN-major layout
-//    that makes it dS, operand A of dQ = dS K.
+//    S^T = K Q^T and dP^T = V dO^T land in TMEM (128 columns each); two
+//    gradient warpgroups (one thread per key, each taking 64 of the 128
+//    query columns: P needs no row reduction since LSE is known) turn them
+//    into P^T and dS^T 32 columns at a time, write both back into columns
+//    the same warp has already read (fp16 pairs, operand A of the next MMAs:
+//    the queries of half h sit at columns 64 h .. 64 h + 31), and write dS^T
+//    to shared memory in the MN-major layout that makes it dS, operand A of
+//    dQ = dS K.
 //  * the MMA warp then issues dV += P^T dO and dK += dS^T Q (A from TMEM,
 //    accumulated over the query tiles in TMEM) and dQ_i = dS K (A and B
 //    from shared memory, K read as MN-major B).
@@ -43,7 +45,7 @@ namespace {
 constexpr int kBM = 128;                  // query rows per tile
 constexpr int kBK = 128;                  // keys per CTA
 constexpr int kD = 64;                    // head dimension
-constexpr int kThreads = 384;             // producer/MMA | gradient | dQ drain
+constexpr int kThreads = 512;             // producer/MMA | gradient x 2 | dQ drain
 constexpr int kTile = 128 * kD * 2;       // 16 KB: one 128 x 64 fp16 tile
 constexpr int kStages = 2;                // (Q, dO, LSE, Delta) ring depth
 constexpr uint32_t kTmemCols = 512;
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       mbar_init(bar_qempty(st), 1);
     }
     mbar_init(bar_s, 1);
-    mbar_init(bar_p, 4);       // one arrival per gradient warp
+    mbar_init(bar_p, 8);       // one arrival per gradient warp
     mbar_init(bar_mm, 1);
     mbar_init(bar_dqfree, 4);  // one arrival per dQ warp
     mbar_init(bar_final, 1);
@@ -229,15 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       tc_fence_after();
       if (elect_one()) {
         // dV += P^T dO and dK += dS^T Q: A from TMEM (16 queries = 8 columns
-        // per K step), B MN-major (16 rows = 2048 B per K step)
+        // per K step; queries 64 h.. at column 64 h), B MN-major (16 rows =
+        // 2048 B per K step)
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ts(tm + kColDV, tm + kColS + kk * 8, d_domn0 + so + 128 * kk, idesc_kv,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tm + kColDV, tm + kColS + 64 * (kk >> 2) + 8 * (kk & 3), d_domn0 + so + 128 * kk,
+                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ts(tm + kColDK, tm + kColDP + kk * 8, d_qmn0 + so + 128 * kk, idesc_kv,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tm + kColDK, tm + kColDP + 64 * (kk >> 2) + 8 * (kk & 3), d_qmn0 + so + 128 * kk,
+                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar_qempty(st));  // Q, dO of this stage are no longer read
       }
       __syncwarp();
@@ -257,9 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     commit_to(bar_final);
     if (lane == 0) mbar_wait_quiet(bar_final, 0);
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
-    // ======================= gradient warpgroup (one thread per key) =======================
-    const int k = threadIdx.x - 128;  // key row within the tile = TMEM lane
+  } else if (warp >= 4 && warp < 12) {
+    // ======================= gradient warpgroups (one thread per key) =======================
+    const int qh = (warp - 4) >> 2;           // query half: columns 64 qh .. 64 qh + 63
+    const int k = 32 * (warp & 3) + lane;     // key row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const uint32_t tS = tmem + lane_base + kColS;
     const uint32_t tDP = tmem + lane_base + kColDP;
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       const float* lse2 = reinterpret_cast<const float*>(smem + kSmemVec + st * 2 * kBM * 4);
       const float* dlt = lse2 + kBM;
 #pragma unroll 1
-      for (int c = 0; c < kBM / 32; ++c) {
+      for (int c = 2 * qh; c < 2 * qh + 2; ++c) {
         uint32_t sr[32], dpr[32];
         tmem_ld32_nowait(tS + 32 * c, sr);
         tmem_ld32_nowait(tDP + 32 * c, dpr);
@@ -301,9 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
           pk_p[e] = pack_f16x2(p0, p1);
           pk_ds[e] = pack_f16x2(ds0, ds1);
         }
-        // P^T and dS^T into columns whose S^T / dP^T values were read already
-        tmem_st16(tS + 16 * c, pk_p);
-        tmem_st16(tDP + 16 * c, pk_ds);
+        // P^T and dS^T into columns this warp has read already: queries
+        // 32c.. at column 64 (c / 2) + 16 (c % 2)
+        tmem_st16(tS + 64 * (c >> 1) + 16 * (c & 1), pk_p);
+        tmem_st16(tDP + 64 * (c >> 1) + 16 * (c & 1), pk_ds);
         // dS^T row k, queries 32c..32c+31: half c / 2, chunks 4 (c % 2) .. +3
         const uint32_t half = ds_row + (c >> 1) * (kTile);
 #pragma unroll
@@ -319,14 +324,14 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p);
     }
-    // ---- dK, dV epilogue ----
+    // ---- dK, dV epilogue (query half 0 writes dV, half 1 dK) ----
     if (ok) ok = warp_wait(bar_final, 0, abort_flag, p.err);
     const int key = kv_start + k;
     if (ok && !*abort_flag) {
       tc_fence_after();
       const long long rowoff = (static_cast<long long>(bh) * p.n + key) * kD;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = qh;
         uint32_t r[64];
         const uint32_t col = tmem + lane_base + (which ? kColDK : kColDV);
         tmem_ld64_wait(col, r);
@@ -343,9 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ======================= dQ drain (one thread per query row) =======================
-    const int t = threadIdx.x - 256;
+    const int t = threadIdx.x - 384;
     const uint32_t tQ = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + kColDQ;
     // staging: two [128 x 32] fp32 halves with the 128-byte swizzle of the
     // dQ tensor map (16-byte chunk c of row t at position c ^ (t % 8))
