@@ -62,8 +62,9 @@ constexpr int kSmemDS = kSmemDO + kStages * kTile;     // dS, 128 x 128 fp16, MN
 constexpr int kSmemDQ = kSmemDS + 2 * kTile;           // dQ staging, 128 x 64 fp32
 constexpr int kSmemVec = kSmemDQ + kBM * kD * 4;       // kStages x (lse2[128], delta[128])
 constexpr int kSmemBar = kSmemVec + kStages * 2 * kBM * 4;
-// kv_full | q_full, q_empty (x kStages) | s_full | p_full | mm_done | dq_free | final
-constexpr int kNumBars = 1 + 2 * kStages + 5;
+// kv_full | q_full, q_empty (x kStages) | s_full, p_full (x 2 query halves) | mm_done |
+// dq_free | final
+constexpr int kNumBars = 1 + 2 * kStages + 7;
 constexpr int kSmemMisc = kSmemBar + kNumBars * 8;     // tmem base, abort flag
 constexpr int kSmemAlloc = kSmemMisc + 16 + 1024;
 static_assert(kSmemAlloc <= 227 * 1024, "shared memory");
@@ -108,11 +109,12 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
   const uint32_t bar_kv = bar0;
   auto bar_qfull = [&](int st) { return bar0 + 8u * (1 + st); };
   auto bar_qempty = [&](int st) { return bar0 + 8u * (1 + kStages + st); };
-  const uint32_t bar_s = bar0 + 8u * (1 + 2 * kStages);     // S^T, dP^T in TMEM
-  const uint32_t bar_p = bar_s + 8;                         // P^T, dS^T written
-  const uint32_t bar_mm = bar_s + 16;                       // all MMAs of a query tile done
-  const uint32_t bar_dqfree = bar_s + 24;                   // dQ columns read out
-  const uint32_t bar_final = bar_s + 32;                    // every MMA of the CTA done
+  const uint32_t bar_x = bar0 + 8u * (1 + 2 * kStages);
+  auto bar_s = [&](int h) { return bar_x + 8u * h; };        // S^T, dP^T of query half h in TMEM
+  auto bar_p = [&](int h) { return bar_x + 8u * (2 + h); };  // P^T, dS^T of half h written
+  const uint32_t bar_mm = bar_x + 32;                       // all MMAs of a query tile done
+  const uint32_t bar_dqfree = bar_x + 40;                   // dQ columns read out
+  const uint32_t bar_final = bar_x + 48;                    // every MMA of the CTA done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
 
@@ -139,8 +141,10 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       mbar_init(bar_qfull(st), 1);
       mbar_init(bar_qempty(st), 1);
     }
-    mbar_init(bar_s, 1);
-    mbar_init(bar_p, 8);       // one arrival per gradient warp
+    for (int hq = 0; hq < 2; ++hq) {
+      mbar_init(bar_s(hq), 1);
+      mbar_init(bar_p(hq), 4);  // one arrival per gradient warp of that half
+    }
     mbar_init(bar_mm, 1);
     mbar_init(bar_dqfree, 4);  // one arrival per dQ warp
     mbar_init(bar_final, 1);
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
     // Warp-uniform operands, one elected lane issues (as in the forward).
-    constexpr uint32_t idesc_s = make_idesc_f16_f32(kBK, kBM, false);          // K-major A, B
+    constexpr uint32_t idesc_s = make_idesc_f16_f32(kBK, kBM / 2, false);      // K-major A, B
     constexpr uint32_t idesc_kv = make_idesc_f16_f32(kBK, kD, true);           // B MN-major
     constexpr uint32_t idesc_dq = make_idesc_f16_f32(kBM, kD, true, true);     // A, B MN-major
     constexpr uint64_t kTileEnc = kTile >> 4;
@@ -217,33 +221,46 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       // columns its P^T / dS^T operands sit in, and dS in shared memory is rewritten
       if (it > 0 && !warp_wait_issuer(bar_mm, (it - 1) & 1, abort_flag, p.err)) break;
       tc_fence_after();
+      // S^T, dP^T one query half at a time (N = 64; half h's queries are the
+      // 8 KB of Q / dO rows 64 h..), so the gradient warps of half 0 start
+      // while half 1 is computed
       if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          umma_f16_ss(tm + kColS, d_k + 2 * kk, d_q0 + so + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+        for (int hq = 0; hq < 2; ++hq) {
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          umma_f16_ss(tm + kColDP, d_v + 2 * kk, d_do0 + so + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit(bar_s);
+          for (int kk = 0; kk < kD / 16; ++kk)
+            umma_f16_ss(tm + kColS + 64 * hq, d_k + 2 * kk, d_q0 + so + 512 * hq + 2 * kk, idesc_s,
+                        kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            umma_f16_ss(tm + kColDP + 64 * hq, d_v + 2 * kk, d_do0 + so + 512 * hq + 2 * kk, idesc_s,
+                        kk > 0 ? 1u : 0u);
+          umma_commit(bar_s(hq));
+        }
       }
       __syncwarp();
-      if (!warp_wait_issuer(bar_p, it & 1, abort_flag, p.err)) break;
-      tc_fence_after();
-      if (elect_one()) {
-        // dV += P^T dO and dK += dS^T Q: A from TMEM (16 queries = 8 columns
-        // per K step; queries 64 h.. at column 64 h), B MN-major (16 rows =
-        // 2048 B per K step)
+      bool done = true;
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ts(tm + kColDV, tm + kColS + 64 * (kk >> 2) + 8 * (kk & 3), d_domn0 + so + 128 * kk,
-                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+      for (int hq = 0; hq < 2; ++hq) {
+        if (!warp_wait_issuer(bar_p(hq), it & 1, abort_flag, p.err)) { done = false; break; }
+        tc_fence_after();
+        if (elect_one()) {
+          // dV += P^T dO and dK += dS^T Q over this half's 64 queries: A from
+          // TMEM (16 queries = 8 columns per K step, half h at column 64 h),
+          // B MN-major (16 rows = 2048 B per K step)
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ts(tm + kColDK, tm + kColDP + 64 * (kk >> 2) + 8 * (kk & 3), d_qmn0 + so + 128 * kk,
-                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar_qempty(st));  // Q, dO of this stage are no longer read
+          for (int kk = 4 * hq; kk < 4 * hq + 4; ++kk)
+            umma_f16_ts(tm + kColDV, tm + kColS + 64 * hq + 8 * (kk & 3), d_domn0 + so + 128 * kk,
+                        idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 4 * hq; kk < 4 * hq + 4; ++kk)
+            umma_f16_ts(tm + kColDK, tm + kColDP + 64 * hq + 8 * (kk & 3), d_qmn0 + so + 128 * kk,
+                        idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          if (hq == 1) umma_commit(bar_qempty(st));  // Q, dO of this stage are no longer read
+        }
+        __syncwarp();
       }
-      __syncwarp();
+      if (!done) break;
       // dQ_i = dS K into the dQ columns once the drain warps have read dQ_{i-1}
       if (it > 0 && !warp_wait_issuer(bar_dqfree, (it - 1) & 1, abort_flag, p.err)) break;
       tc_fence_after();
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       const int st = it % kStages;
       const int qi = i0 + it;
       const bool diag = kCausal && qi == jt;  // keys after a query are masked
-      if (!warp_wait(bar_s, it & 1, abort_flag, p.err)) { ok = false; break; }
+      if (!warp_wait(bar_s(qh), it & 1, abort_flag, p.err)) { ok = false; break; }
       // (the stage's LSE / Delta vectors came by TMA: observe their barrier too)
       if (!warp_wait(bar_qfull(st), (it / kStages) & 1, abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
@@ -322,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       fence_proxy_async_smem();  // dS in shared memory is read by the tensor core
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p);
+      if (lane == 0) mbar_arrive(bar_p(qh));
     }
     // ---- dK, dV epilogue (query half 0 writes dV, half 1 dK) ----
     if (ok) ok = warp_wait(bar_final, 0, abort_flag, p.err);
