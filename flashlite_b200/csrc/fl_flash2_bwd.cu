@@ -58,8 +58,8 @@ constexpr int kSmemK = 0;
 constexpr int kSmemV = kSmemK + kTile;
 constexpr int kSmemQ = kSmemV + kTile;                 // kStages tiles
 constexpr int kSmemDO = kSmemQ + kStages * kTile;      // kStages tiles
-constexpr int kSmemDS = kSmemDO + kStages * kTile;     // dS, 128 x 128 fp16, MN-major
-constexpr int kSmemDQ = kSmemDS + 2 * kTile;           // dQ staging, 128 x 64 fp32
+constexpr int kSmemDS = kSmemDO + kStages * kTile;     // 2 x dS, 128 x 128 fp16, MN-major
+constexpr int kSmemDQ = kSmemDS + 4 * kTile;           // dQ staging, 128 x 64 fp32
 constexpr int kSmemVec = kSmemDQ + kBM * kD * 4;       // kStages x (lse2[128], delta[128])
 constexpr int kSmemBar = kSmemVec + kStages * 2 * kBM * 4;
 // kv_full | q_full, q_empty (x kStages) | s_full, p_full (x 2 query halves) | mm_done |
@@ -212,18 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       if (elect_one()) umma_commit(bar);
       __syncwarp();
     };
-    bool ok = warp_wait_issuer(bar_kv, 0, abort_flag, p.err);
-    for (int it = 0; ok && it < nq; ++it) {
-      const int st = it % kStages;
-      const uint64_t so = static_cast<uint64_t>(st) * kTileEnc;
-      if (!warp_wait_issuer(bar_qfull(st), (it / kStages) & 1, abort_flag, p.err)) break;
-      // the previous query tile's MMAs must be done: S^T / dP^T overwrite the
-      // columns its P^T / dS^T operands sit in, and dS in shared memory is rewritten
-      if (it > 0 && !warp_wait_issuer(bar_mm, (it - 1) & 1, abort_flag, p.err)) break;
-      tc_fence_after();
-      // S^T, dP^T one query half at a time (N = 64; half h's queries are the
-      // 8 KB of Q / dO rows 64 h..), so the gradient warps of half 0 start
-      // while half 1 is computed
+    // S^T, dP^T of query tile `it`, one query half at a time (N = 64; half h's
+    // queries are the 8 KB of Q / dO rows 64 h..), so the gradient warps of
+    // half 0 start while half 1 is computed
+    auto issue_s = [&](int it) {
+      const uint64_t so = static_cast<uint64_t>(it % kStages) * kTileEnc;
       if (elect_one()) {
 #pragma unroll
         for (int hq = 0; hq < 2; ++hq) {
@@ -239,6 +232,19 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
         }
       }
       __syncwarp();
+    };
+    bool ok = warp_wait_issuer(bar_kv, 0, abort_flag, p.err) &&
+              warp_wait_issuer(bar_qfull(0), 0, abort_flag, p.err);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+    }
+    // Per query tile i: dV, dK of i (as its gradient halves finish), then
+    // S^T, dP^T of tile i + 1, then dQ_i, so the gradient warps of tile i + 1
+    // work while dQ_i is computed (dS is double-buffered in shared memory).
+    for (int it = 0; ok && it < nq; ++it) {
+      const int st = it % kStages;
+      const uint64_t so = static_cast<uint64_t>(st) * kTileEnc;
       bool done = true;
 #pragma unroll
       for (int hq = 0; hq < 2; ++hq) {
@@ -256,18 +262,28 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
           for (int kk = 4 * hq; kk < 4 * hq + 4; ++kk)
             umma_f16_ts(tm + kColDK, tm + kColDP + 64 * hq + 8 * (kk & 3), d_qmn0 + so + 128 * kk,
                         idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-          if (hq == 1) umma_commit(bar_qempty(st));  // Q, dO of this stage are no longer read
+          // dV, dK of this tile done: Q, dO of the stage and the TMEM columns
+          // of P^T, dS^T are free
+          if (hq == 1) umma_commit(bar_qempty(st));
         }
         __syncwarp();
       }
       if (!done) break;
-      // dQ_i = dS K into the dQ columns once the drain warps have read dQ_{i-1}
+      if (it + 1 < nq) {
+        if (!warp_wait_issuer(bar_qfull((it + 1) % kStages), ((it + 1) / kStages) & 1, abort_flag, p.err) ||
+            !warp_wait_issuer(bar_qempty(st), (it / kStages) & 1, abort_flag, p.err))
+          break;
+        tc_fence_after();
+        issue_s(it + 1);
+      }
+      // dQ_i = dS_i K (dS buffer i % 2) once the drain warps have read dQ_{i-1}
       if (it > 0 && !warp_wait_issuer(bar_dqfree, (it - 1) & 1, abort_flag, p.err)) break;
       tc_fence_after();
       if (elect_one()) {
+        const uint64_t dsb = d_ds + static_cast<uint64_t>(it & 1) * ((4 * kTile / 2) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16_ss(tm + kColDQ, d_ds + 128 * kk, d_kmn + 128 * kk, idesc_dq, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tm + kColDQ, dsb + 128 * kk, d_kmn + 128 * kk, idesc_dq, kk > 0 ? 1u : 0u);
         umma_commit(bar_mm);
       }
       __syncwarp();
@@ -288,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     // dS^T row k is column k of dS: in the MN-major operand it is row k % 8 of
     // 8-key group k / 8; 16-byte chunk c (queries 8c..8c+7 of a 64-query half)
     // sits at position c ^ (k % 8) (128-byte swizzle)
-    const uint32_t ds_row = s_ds + (k >> 3) * 1024 + (k & 7) * 128;
+    const uint32_t ds_row0 = s_ds + (k >> 3) * 1024 + (k & 7) * 128;
     bool ok = true;
     for (int it = 0; ok && it < nq; ++it) {
       const int st = it % kStages;
@@ -299,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       if (!warp_wait(bar_qfull(st), (it / kStages) & 1, abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
       const float* lse2 = reinterpret_cast<const float*>(smem + kSmemVec + st * 2 * kBM * 4);
+      const uint32_t ds_row = ds_row0 + (it & 1) * (2 * kTile);  // dS buffer of this tile
       const float* dlt = lse2 + kBM;
 #pragma unroll 1
       for (int c = 2 * qh; c < 2 * qh + 2; ++c) {
