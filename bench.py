@@ -1,7 +1,10 @@
 """Benchmark of the FA2 forward hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg3|cfg3c|cfg2|cfg2c|cfg4]
+                    [--workload cfg3|cfg3c|cfg2|cfg2c|cfg4|cfg5|bwd3|bwd3c|d128_3|d128_3c]
+
+(bwd3/bwd3c: the backward pass, d128_3/d128_3c: the head_dim-128 forward, on
+the config-3 shape; extensions without a reference counterpart.)
 
 Metric: FA2 forward TFLOP/s per B200 (fp16, D=64), FLOPs =
 4·B·H·N²·D halved for causal (reference benchmarks/benchmark_throughput.py:23-31).
@@ -49,6 +52,15 @@ WORKLOADS = {
     "cfg3c": (2, 8, 4096, True, "BASELINE config 3: B2 H8 N4096 D64 causal"),
     "cfg4": (16, 32, 8192, True, "BASELINE config 4: B16 H32 N8192 D64 causal, 512 slices split over ranks"),
     "cfg5": (1, 8, 131072, True, "BASELINE config 5: B1 H8 N131072 D64 causal, sequence sharded, NCCL ring"),
+}
+
+# Extension workloads (no reference counterpart: the reference is forward-only
+# and head_dim 64 only): name -> (B, H, N, D, causal, backward, description)
+EXT_WORKLOADS = {
+    "bwd3": (2, 8, 4096, 64, False, True, "FA2 backward on the config-3 shape: B2 H8 N4096 D64 non-causal"),
+    "bwd3c": (2, 8, 4096, 64, True, True, "FA2 backward on the config-3 shape: B2 H8 N4096 D64 causal"),
+    "d128_3": (2, 8, 4096, 128, False, False, "FA2 forward, head_dim 128: B2 H8 N4096 D128 non-causal"),
+    "d128_3c": (2, 8, 4096, 128, True, False, "FA2 forward, head_dim 128: B2 H8 N4096 D128 causal"),
 }
 
 
@@ -375,6 +387,128 @@ def run_ours(args):
 
 
 # ----------------------------------------------------------------------------
+# extension workloads: backward, head_dim 128 (single GPU or weak-scaled copies)
+# ----------------------------------------------------------------------------
+def run_ext(args):
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    init_dist(world, "nccl")
+    from flashlite_b200 import flash_attn_wmma as fa
+
+    B, H, N, D, causal, bwd, desc = EXT_WORKLOADS[args.workload]
+    sm_scale = 0.0  # 1/sqrt(D)
+    g = torch.Generator().manual_seed(7 + rank)
+    host = [torch.randn(B, H, N, D, generator=g).half() for _ in range(4 if bwd else 3)]
+    tensor_bytes = host[0].numel() * 2
+    in_bytes = (6 if bwd else 3) * tensor_bytes  # bwd: q, k, v, out, dout (+ lse)
+    n_sets = max(2, math.ceil(3 * L2_BYTES / in_bytes))
+    sets = []
+    for i in range(n_sets):
+        q, k, v = (t.to(device) for t in host[:3])
+        if bwd:
+            do = host[3].to(device)
+            out, lse = fa.forward_flash2_ex(q, k, v, sm_scale, causal, return_lse=True)
+            sets.append((q, k, v, out, do, lse))
+        else:
+            sets.append((q, k, v, torch.empty_like(q)))
+    stream = torch.cuda.current_stream(device)
+
+    def step(i):
+        t = sets[i % n_sets]
+        if bwd:
+            return fa.backward_flash2(*t, sm_scale, causal)
+        return fa.forward_flash2_ex(t[0], t[1], t[2], sm_scale, causal, out=t[3])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world, device)
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1), world, device) / args.steps
+    err = fa.device_error()
+    # FLOPs: forward 4·B·H·N²·D (halved causal); backward 2.5x that (five GEMMs to two)
+    f_step = (2.5 if bwd else 1.0) * flops(B, H, N, D, causal)
+    value = world * f_step / (ms_step * 1e-3) / 1e12
+
+    # end to end through the public API: inputs from pinned host memory, the
+    # results (dq, dk, dv or out) read back each step, serially
+    pinned = [t.pin_memory() for t in host]
+    dev = [torch.empty_like(t, device=device) for t in host]
+    lse_h = sets[0][5].cpu().pin_memory() if bwd else None
+    out_h = sets[0][3].cpu().pin_memory() if bwd else None
+    lse_d = torch.empty_like(sets[0][5]) if bwd else None
+    out_d = torch.empty_like(sets[0][3]) if bwd else None
+    res_h = [torch.empty_like(host[0]).pin_memory() for _ in range(3 if bwd else 1)]
+
+    def e2e(n):
+        for _ in range(n):
+            for d_, h_ in zip(dev, pinned):
+                d_.copy_(h_, non_blocking=True)
+            if bwd:
+                out_d.copy_(out_h, non_blocking=True)
+                lse_d.copy_(lse_h, non_blocking=True)
+                res = fa.backward_flash2(dev[0], dev[1], dev[2], out_d, dev[3], lse_d, sm_scale, causal)
+            else:
+                res = (fa.forward_flash2_ex(dev[0], dev[1], dev[2], sm_scale, causal)[0],)
+            for r_h, r in zip(res_h, res):
+                r_h.copy_(r, non_blocking=True)
+
+    e_steps = max(3, min(args.steps, 30))
+    e2e(3)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    e2e(e_steps)
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    e_ms = max_over_ranks(t0.elapsed_time(t1) / e_steps, world, device)
+    h2d = sum(t.numel() * t.element_size() for t in host) + (
+        (out_h.numel() * 2 + lse_h.numel() * 4) if bwd else 0)
+    d2h = sum(t.numel() * 2 for t in res_h)
+
+    peak_burst, peak_sust, hbm, peak_kind = measured_peaks()
+    achieved = f_step / (ms_step * 1e-3) / 1e12
+    kernel = "flash2_bwd" if bwd else "flash2_fwd"
+    if rank == 0:
+        line = {
+            "metric": ("FA2 bwd" if bwd else "FA2 fwd") + f" TFLOP/s per B200 (fp16, D={D})",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+            "data": "synthetic: seeded i.i.d. N(0,1) fp16 inputs generated on host",
+            "config": {"workload": desc, "B": B, "H": H, "N": N, "D": D, "causal": causal,
+                       "sm_scale": "1/sqrt(D)",
+                       "flops_per_step": f_step,
+                       "parallelism": f"independent copies x{world}" if world > 1 else "single GPU",
+                       "l2": f"{n_sets} rotating input sets, {n_sets * in_bytes / 2**20:.0f} MiB > 126 MB L2"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_burst,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak_burst, 4),
+                         "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
+                         "traffic": profiled_traffic(kernel, args.workload)},
+            "e2e": {"value": round(world * f_step / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 4),
+                    "mode": "serial: copies in, the call, results out"},
+            "gpu_launches": args.steps * (3 if bwd else 1),
+            "clocks": clk.summary(),
+            "device_error": int(err),
+            "cpu_baseline": None,
+            "note": "no reference counterpart (the reference is forward-only and head_dim 64 only)",
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
 # config 5: sequence-sharded ring attention (strong scaling over ranks)
 # ----------------------------------------------------------------------------
 def run_ring(args):
@@ -630,7 +764,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg3", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cfg3", choices=sorted(WORKLOADS) + sorted(EXT_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ring-layout", default="zigzag", choices=["zigzag", "contiguous"],
                     help="sequence layout of the config-5 ring on 2+ GPUs")
@@ -640,8 +774,14 @@ def main():
     world, _, _ = dist_env()
     if world != args.gpus and not (world == 1 and args.gpus == 1):
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
-    if args.impl == "reference":
+    if args.impl == "reference" and args.workload in EXT_WORKLOADS:
+        if dist_env()[1] == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference is forward-only and "
+                              "takes head_dim 64 only: no counterpart for " + args.workload}))
+    elif args.impl == "reference":
         run_reference(args)
+    elif args.workload in EXT_WORKLOADS:
+        run_ext(args)
     elif args.workload == "cfg5":
         run_ring(args)
     else:
