@@ -15,7 +15,8 @@ FL_OK, FL_ERR_INVALID_ARGUMENT, FL_ERR_UNSUPPORTED = 0, 1, 2
 
 def test_header_declares_expected_api(header_fns):
     for name in ("fl_flash2_fwd", "fl_naive_fwd", "fl_flash2_fwd_block", "fl_ring_finalize",
-                 "fl_status_str", "fl_last_error", "fl_device_error", "fl_version"):
+                 "fl_status_str", "fl_last_error", "fl_device_error", "fl_version",
+                 "fl_flash2_fwd_ex", "fl_flash2_bwd", "fl_flash2_bwd_workspace_size"):
         assert name in header_fns
 
 
@@ -86,3 +87,33 @@ def test_package_refuses_to_import_without_native_code(tmp_path, monkeypatch):
     # binding's own builtins
     assert type(fa.forward_flash2).__name__ == "builtin_function_or_method"
     assert type(fa.forward_naive).__name__ == "builtin_function_or_method"
+
+
+def test_backward_checks_before_device(fl_lib):
+    # fl_flash2_bwd validates pointers, head_dim and the workspace size
+    # before it looks for a device
+    vp, i64, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t
+    fl_lib.fl_flash2_bwd_workspace_size.argtypes = [i64, i64, i64, i64]
+    fl_lib.fl_flash2_bwd_workspace_size.restype = sz
+    fl_lib.fl_flash2_bwd.argtypes = [vp] * 10 + [sz, i64, i64, i64, i64, ctypes.c_float, ctypes.c_int, vp]
+    need = fl_lib.fl_flash2_bwd_workspace_size(2, 8, 1000, 64)
+    # fp32 dQ accumulator + two per-row vectors padded to 128-row tiles
+    assert need == (2 * 8 * 1000 * 64 + 2 * 2 * 8 * 1024) * 4
+    assert fl_lib.fl_flash2_bwd_workspace_size(2, 8, 1000, 128) == 0
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+    args = [p] * 10
+    assert fl_lib.fl_flash2_bwd(*([None] * 10), 0, 1, 1, 128, 64, 0.0, 0, None) == FL_ERR_INVALID_ARGUMENT
+    assert fl_lib.fl_flash2_bwd(*args, 4096, 1, 1, 128, 128, 0.0, 0, None) == FL_ERR_UNSUPPORTED
+    assert b"head_dim == 64" in fl_lib.fl_last_error()
+    assert fl_lib.fl_flash2_bwd(*args, 16, 1, 1, 128, 64, 0.0, 0, None) == FL_ERR_INVALID_ARGUMENT
+    assert b"workspace too small" in fl_lib.fl_last_error()
+    assert fl_lib.fl_flash2_bwd(*args, 0, 0, 1, 128, 64, 0.0, 0, None) == FL_OK  # empty batch
+
+
+def test_backward_binding_rejects_cpu_tensors():
+    q, k, v = _qkv()
+    lse = torch.zeros(1, 2, 128)
+    with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
+        fa.backward_flash2(q, k, v, q, q, lse)
+    assert "is_causal" in fa.backward_flash2.__doc__ and "sm_scale" in fa.backward_flash2.__doc__

@@ -187,3 +187,21 @@ def test_ring_peer_failure_is_an_error_not_a_hang():
             pytest.fail("a surviving rank hung instead of raising")
     assert results[1] == "raised"
     assert str(results[0]).startswith("error"), results[0]
+
+
+def test_bench_reference_arm_for_extensions_is_unavailable():
+    # the backward and head_dim-128 workloads have no reference counterpart:
+    # the reference arm prints its `unavailable` line and exits 0
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    for w in ("bwd3", "d128_3"):
+        r = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference", "--workload", w,
+                            "--steps", "1", "--warmup", "3"], capture_output=True, text=True, timeout=300,
+                           cwd=str(root))
+        assert r.returncode == 0, r.stderr
+        line = json.loads(r.stdout.strip().splitlines()[-1])
+        assert line["impl"] == "reference" and "unavailable" in line
