@@ -251,10 +251,12 @@ size_t fl_flash2_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D) 
 int fl_flash2_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                   const float* lse, void* dq, void* dk, void* dv, void* workspace,
                   size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D,
-                  float sm_scale, int is_causal, void* stream) {
+                  float sm_scale, int is_causal, int layout, void* stream) {
   int st = check_common(q, k, v, o, B, H, N, D);
   if (st != FL_OK) return st;
   if (!dout || !lse || !dq || !dk || !dv) return fail(FL_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (layout != FL_LAYOUT_BHND && layout != FL_LAYOUT_BNHD)
+    return fail(FL_ERR_INVALID_ARGUMENT, "unknown layout");
   if (D != 64) return fail(FL_ERR_UNSUPPORTED, "backward_flash2 requires head_dim == 64");
   if (B == 0 || H == 0 || N == 0) return FL_OK;
   if (B * H > (1LL << 30)) return fail(FL_ERR_INVALID_ARGUMENT, "dimension too large");
@@ -273,7 +275,7 @@ int fl_flash2_bwd(const void* q, const void* k, const void* v, const void* o, co
   const char* where = "flash2 backward";
   cudaError_t e = fl::launch_flash2_bwd(q, k, v, o, dout, lse, dq, dk, dv, workspace, B, H, N,
                                         static_cast<float>(scale), is_causal != 0,
-                                        static_cast<cudaStream_t>(stream), &where);
+                                        layout == FL_LAYOUT_BNHD, static_cast<cudaStream_t>(stream), &where);
   if (e != cudaSuccess) return cuda_fail(e, (std::string("flash2 backward: ") + where).c_str());
   return FL_OK;
 }

@@ -74,10 +74,11 @@ struct BwdParams {
   CUtensorMap tm_dq;                    // fp32 {64, N, H, B} dQ accumulator, box {32, 128}, SW128
   const float* lse2;   // [BH, npad] LSE * log2(e), +inf past N
   const float* delta;  // [BH, npad] rowsum(dO * O), 0 past N
-  __half* dk;          // [BH, N, 64]
-  __half* dv;          // [BH, N, 64]
+  __half* dk;          // [B, H, N, 64] (bnhd: [B, N, H, 64])
+  __half* dv;
   unsigned int* err;
   int n, npad, bh, nh, n_tiles;
+  int bnhd;            // layout of q, k, v, o, dout, dq, dk, dv
   float scale_log2;    // sm_scale * log2(e)
   float scale;         // sm_scale
 };
@@ -370,7 +371,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     const int key = kv_start + k;
     if (ok && !*abort_flag) {
       tc_fence_after();
-      const long long rowoff = (static_cast<long long>(bh) * p.n + key) * kD;
+      const long long rowoff =
+          (p.bnhd ? (static_cast<long long>(b) * p.n + key) * p.nh + h
+                  : static_cast<long long>(bh) * p.n + key) * kD;
       {
         const int which = qh;
         uint32_t r[64];
@@ -435,10 +438,12 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
 
 // Delta = rowsum(dO * O) and lse2 = LSE * log2(e) per query row, padded to
 // whole 128-row tiles (Delta 0 and lse2 +inf past N: those rows get p = 0).
-// Eight threads per row, 16 bytes of O and dO each.
+// Eight threads per row, 16 bytes of O and dO each. LSE is [B, H, N] in
+// either layout.
 __global__ void flash2_bwd_prep_kernel(const __half* __restrict__ o, const __half* __restrict__ dout,
                                        const float* __restrict__ lse, float* __restrict__ lse2,
-                                       float* __restrict__ delta, int n, int npad, long long rows) {
+                                       float* __restrict__ delta, int n, int npad, long long rows,
+                                       int nh, int bnhd) {
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long row = gid >> 3;
   const int sub = threadIdx.x & 7;
@@ -447,7 +452,8 @@ __global__ void flash2_bwd_prep_kernel(const __half* __restrict__ o, const __hal
   const int r = valid_row ? static_cast<int>(row - bh * npad) : 0;
   float d = 0.0f;
   if (valid_row && r < n) {
-    const long long off = (bh * n + r) * kD + sub * 8;
+    const long long row_elem = bnhd ? ((bh / nh) * n + r) * nh + bh % nh : bh * n + r;
+    const long long off = row_elem * kD + sub * 8;
     const uint4 a = *reinterpret_cast<const uint4*>(o + off);
     const uint4 g = *reinterpret_cast<const uint4*>(dout + off);
     const __half2* ah = reinterpret_cast<const __half2*>(&a);
@@ -469,13 +475,16 @@ __global__ void flash2_bwd_prep_kernel(const __half* __restrict__ o, const __hal
   }
 }
 
-bool encode_dq_map(CUtensorMap* tm, float* base, int64_t n, int64_t H, int64_t B) {
+// fp32 map {64, N, H, B} over the dQ accumulator, laid out like dq itself
+// ([B,H,N,64] or, with bnhd, [B,N,H,64]) so the final cast is elementwise.
+bool encode_dq_map(CUtensorMap* tm, float* base, int64_t n, int64_t H, int64_t B, bool bnhd) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const cuuint64_t row_b = kD * 4;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(n),
                         static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[3] = {row_b, static_cast<cuuint64_t>(n) * row_b,
+  cuuint64_t strides[3] = {bnhd ? H * row_b : row_b,
+                           bnhd ? row_b : static_cast<cuuint64_t>(n) * row_b,
                            static_cast<cuuint64_t>(n) * H * row_b};
   cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kBM), 1, 1};  // 128-byte rows
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -509,7 +518,7 @@ size_t flash2_bwd_workspace_bytes(int64_t BH, int64_t N) {
 cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const void* o,
                               const void* dout, const float* lse, void* dq, void* dk, void* dv,
                               void* workspace, int64_t B, int64_t H, int64_t N, float sm_scale,
-                              bool causal, cudaStream_t stream, const char** where) {
+                              bool causal, bool bnhd, cudaStream_t stream, const char** where) {
   const int64_t BH = B * H;
   const int64_t npad = (N + kBM - 1) / kBM * kBM;
   float* dq_acc = static_cast<float*>(workspace);
@@ -517,11 +526,11 @@ cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const
   float* delta = lse2 + BH * npad;
   BwdParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  if (!encode_rows_map(&prm.tm_q, q, N, H, B, false, kD, kBM) ||
-      !encode_rows_map(&prm.tm_k, k, N, H, B, false, kD, kBK) ||
-      !encode_rows_map(&prm.tm_v, v, N, H, B, false, kD, kBK) ||
-      !encode_rows_map(&prm.tm_do, dout, N, H, B, false, kD, kBM) ||
-      !encode_dq_map(&prm.tm_dq, dq_acc, N, H, B)) {
+  if (!encode_rows_map(&prm.tm_q, q, N, H, B, bnhd, kD, kBM) ||
+      !encode_rows_map(&prm.tm_k, k, N, H, B, bnhd, kD, kBK) ||
+      !encode_rows_map(&prm.tm_v, v, N, H, B, bnhd, kD, kBK) ||
+      !encode_rows_map(&prm.tm_do, dout, N, H, B, bnhd, kD, kBM) ||
+      !encode_dq_map(&prm.tm_dq, dq_acc, N, H, B, bnhd)) {
     *where = "tensor map encoding";
     return cudaErrorInvalidValue;
   }
@@ -534,7 +543,7 @@ cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const
   const long long blocks = (rows * 8 + threads - 1) / threads;
   flash2_bwd_prep_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
       static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, lse2, delta,
-      static_cast<int>(N), static_cast<int>(npad), rows);
+      static_cast<int>(N), static_cast<int>(npad), rows, static_cast<int>(H), bnhd ? 1 : 0);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   prm.lse2 = lse2;
@@ -546,6 +555,7 @@ cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const
   prm.npad = static_cast<int>(npad);
   prm.bh = static_cast<int>(BH);
   prm.nh = static_cast<int>(H);
+  prm.bnhd = bnhd ? 1 : 0;
   prm.n_tiles = static_cast<int>(npad / kBM);
   prm.scale = sm_scale;
   prm.scale_log2 = static_cast<float>(sm_scale * 1.44269504088896340736);

@@ -44,14 +44,14 @@ cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f
                           bool merge, bool first, bool bnhd, cudaStream_t stream,
                           int head_dim = 64);
 
-// FA2 backward (head_dim 64, [B,H,N,64] fp16): dq, dk, dv from q, k, v, the
+// FA2 backward (head_dim 64, [B,H,N,64] or with bnhd [B,N,H,64] fp16): dq, dk, dv from q, k, v, the
 // forward output o, its gradient dout and the forward's natural-log LSE
 // [B,H,N] fp32. workspace: flash2_bwd_workspace_bytes(B*H, N) bytes.
 size_t flash2_bwd_workspace_bytes(int64_t BH, int64_t N);
 cudaError_t launch_flash2_bwd(const void* q, const void* k, const void* v, const void* o,
                               const void* dout, const float* lse, void* dq, void* dk, void* dv,
                               void* workspace, int64_t B, int64_t H, int64_t N, float sm_scale,
-                              bool causal, cudaStream_t stream, const char** where);
+                              bool causal, bool bnhd, cudaStream_t stream, const char** where);
 
 cudaError_t launch_naive(const void* q, const void* k, const void* v, void* o, int64_t BH,
                          int64_t N, int64_t D, float sm_scale, bool causal, cudaStream_t stream);

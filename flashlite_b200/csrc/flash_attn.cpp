@@ -196,20 +196,23 @@ int64_t device_error() {
 
 // FA2 backward (no reference counterpart): gradients of
 // softmax(sm_scale * q k^T) v given the forward output `out`, its gradient
-// `dout` and the forward's LSE (forward_flash2_ex(..., return_lse=True)).
+// `dout` and the forward's LSE (forward_flash2_ex(..., return_lse=True));
+// layout "bnhd" takes [B, N, H, D] tensors (lse stays [B, H, N]).
 // Returns (dq, dk, dv); the fp32 workspace is a torch allocation.
 std::vector<torch::Tensor> backward_flash2(torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                            torch::Tensor out, torch::Tensor dout, torch::Tensor lse,
-                                           double sm_scale, bool is_causal) {
+                                           double sm_scale, bool is_causal, std::string layout) {
+  TORCH_CHECK(layout == "bhnd" || layout == "bnhd", "layout must be 'bhnd' or 'bnhd'");
+  const bool bnhd = layout == "bnhd";
   for (const torch::Tensor* t : {&q, &k, &v, &out, &dout}) {
     TORCH_CHECK(t->is_cuda(), "All tensors must be on CUDA");
     TORCH_CHECK(t->is_contiguous(), "All tensors must be contiguous");
     TORCH_CHECK(t->dtype() == torch::kHalf, "q, k, v, out and dout must be FP16 (Half)");
-    TORCH_CHECK(t->dim() == 4, "Tensors must be 4D [B, H, N, D]");
-    TORCH_CHECK(t->sizes() == q.sizes(), "q, k, v, out and dout must have the same shape [B, H, N, D]");
+    TORCH_CHECK(t->dim() == 4, bnhd ? "Tensors must be 4D [B, N, H, D]" : "Tensors must be 4D [B, H, N, D]");
+    TORCH_CHECK(t->sizes() == q.sizes(), "q, k, v, out and dout must have the same shape");
     TORCH_CHECK(t->device() == q.device(), "All tensors must be on the same CUDA device");
   }
-  const int64_t B = q.size(0), H = q.size(1), N = q.size(2), D = q.size(3);
+  const int64_t B = q.size(0), H = q.size(bnhd ? 2 : 1), N = q.size(bnhd ? 1 : 2), D = q.size(3);
   TORCH_CHECK(D == 64, "backward_flash2 requires head_dim == 64");
   TORCH_CHECK(lse.is_cuda() && lse.is_contiguous() && lse.dtype() == torch::kFloat &&
                   lse.device() == q.device(),
@@ -223,7 +226,7 @@ std::vector<torch::Tensor> backward_flash2(torch::Tensor q, torch::Tensor k, tor
   check_status(fl_flash2_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
                              lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                              ws.data_ptr(), ws_bytes, B, H, N, D, static_cast<float>(sm_scale),
-                             is_causal ? 1 : 0, stream_of(q)));
+                             is_causal ? 1 : 0, bnhd ? FL_LAYOUT_BNHD : FL_LAYOUT_BHND, stream_of(q)));
   return {dq, dk, dv};
 }
 
@@ -251,6 +254,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("backward_flash2", &backward_flash2,
         "FA2 backward (tcgen05, sm_100a); returns (dq, dk, dv)", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("sm_scale") = 0.0,
-        py::arg("is_causal") = false);
+        py::arg("is_causal") = false, py::arg("layout") = "bhnd");
   m.def("device_error", &device_error, "Read and clear kernel error flags (synchronises)");
 }

@@ -44,7 +44,7 @@ typedef enum fl_status {
 int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
                   int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);
 
-/* Tensor layouts accepted by fl_flash2_fwd_ex. */
+/* Tensor layouts accepted by fl_flash2_fwd_ex and fl_flash2_bwd. */
 enum fl_layout {
   FL_LAYOUT_BHND = 0, /* [B, H, N, D]: the reference's layout */
   FL_LAYOUT_BNHD = 1  /* [B, N, H, D]: the flash_attn package's layout */
@@ -70,8 +70,9 @@ int fl_flash2_fwd_ex(const void* q, const void* k, const void* v, void* o, float
 
 /*
  * FA2 backward; no reference counterpart (the reference is forward-only).
- * q, k, v, o, dout, dq, dk, dv: [B, H, N, 64] fp16 (o = the forward output,
- * dout = dL/do); lse: [B, H, N] fp32, the natural-log log-sum-exp the
+ * q, k, v, o, dout, dq, dk, dv: [B, H, N, 64] fp16, or [B, N, H, 64] with
+ * layout FL_LAYOUT_BNHD (o = the forward output, dout = dL/do); lse:
+ * [B, H, N] fp32 in either layout, the natural-log log-sum-exp the
  * forward returns (fl_flash2_fwd_ex with a non-NULL lse). Computes dq, dk,
  * dv of softmax(sm_scale * q k^T [causal mask]) v; sm_scale == 0 means
  * 1/sqrt(64). workspace: device memory of at least
@@ -82,7 +83,7 @@ size_t fl_flash2_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D);
 int fl_flash2_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                   const float* lse, void* dq, void* dk, void* dv, void* workspace,
                   size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D,
-                  float sm_scale, int is_causal, void* stream);
+                  float sm_scale, int is_causal, int layout, void* stream);
 
 /*
  * Naive (unfused, fp32 CUDA-core) attention forward, any D in [1, 1024].

@@ -95,7 +95,7 @@ def test_backward_checks_before_device(fl_lib):
     vp, i64, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t
     fl_lib.fl_flash2_bwd_workspace_size.argtypes = [i64, i64, i64, i64]
     fl_lib.fl_flash2_bwd_workspace_size.restype = sz
-    fl_lib.fl_flash2_bwd.argtypes = [vp] * 10 + [sz, i64, i64, i64, i64, ctypes.c_float, ctypes.c_int, vp]
+    fl_lib.fl_flash2_bwd.argtypes = [vp] * 10 + [sz, i64, i64, i64, i64, ctypes.c_float, ctypes.c_int, ctypes.c_int, vp]
     need = fl_lib.fl_flash2_bwd_workspace_size(2, 8, 1000, 64)
     # fp32 dQ accumulator + two per-row vectors padded to 128-row tiles
     assert need == (2 * 8 * 1000 * 64 + 2 * 2 * 8 * 1024) * 4
@@ -103,12 +103,12 @@ def test_backward_checks_before_device(fl_lib):
     buf = ctypes.create_string_buffer(4096)
     p = ctypes.addressof(buf)
     args = [p] * 10
-    assert fl_lib.fl_flash2_bwd(*([None] * 10), 0, 1, 1, 128, 64, 0.0, 0, None) == FL_ERR_INVALID_ARGUMENT
-    assert fl_lib.fl_flash2_bwd(*args, 4096, 1, 1, 128, 128, 0.0, 0, None) == FL_ERR_UNSUPPORTED
+    assert fl_lib.fl_flash2_bwd(*([None] * 10), 0, 1, 1, 128, 64, 0.0, 0, 0, None) == FL_ERR_INVALID_ARGUMENT
+    assert fl_lib.fl_flash2_bwd(*args, 4096, 1, 1, 128, 128, 0.0, 0, 0, None) == FL_ERR_UNSUPPORTED
     assert b"head_dim == 64" in fl_lib.fl_last_error()
-    assert fl_lib.fl_flash2_bwd(*args, 16, 1, 1, 128, 64, 0.0, 0, None) == FL_ERR_INVALID_ARGUMENT
+    assert fl_lib.fl_flash2_bwd(*args, 16, 1, 1, 128, 64, 0.0, 0, 0, None) == FL_ERR_INVALID_ARGUMENT
     assert b"workspace too small" in fl_lib.fl_last_error()
-    assert fl_lib.fl_flash2_bwd(*args, 0, 0, 1, 128, 64, 0.0, 0, None) == FL_OK  # empty batch
+    assert fl_lib.fl_flash2_bwd(*args, 0, 0, 1, 128, 64, 0.0, 0, 0, None) == FL_OK  # empty batch
 
 
 def test_backward_binding_rejects_cpu_tensors():
