@@ -230,13 +230,47 @@ __device__ __forceinline__ int produce_ring(const CUtensorMap* tm, uint32_t s_ri
   return issued;
 }
 
+// Split-KV variant: slot 0 streams KV tiles [0, nkv0) and slot 1 tiles
+// [kvb1, kvb1 + nkv1) of the same query tile; both sequences share one ring,
+// interleaved (slot 0's step j, then slot 1's step j), so ring index 2j + i.
+template <int HD, int kStages>
+__device__ __forceinline__ int produce_ring_split(const CUtensorMap* tm, uint32_t s_ring, uint32_t bar_full0,
+                                                  uint32_t bar_empty0, int nkv0, int nkv1, int kvb1, int h,
+                                                  int b, int lane, volatile int* abort_flag, unsigned int* err) {
+  using C = Cfg<HD>;
+  int issued = 0;
+  for (int j = 0; j < nkv0; ++j) {
+    for (int i = 0; i < 2; ++i) {
+      if (i == 1 && j >= nkv1) break;
+      const int t = issued;
+      const int st = t % kStages;
+      const uint32_t ph = (t / kStages) & 1;
+      if (!warp_wait(bar_empty0 + 8u * st, ph ^ 1, abort_flag, err)) return issued;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_full0 + 8u * st, C::kKVTileBytes);
+#pragma unroll
+        for (int hh = 0; hh < C::kHalves; ++hh)
+          tma_load_4d(s_ring + st * C::kKVTileBytes + hh * (C::kBN * 128), tm, bar_full0 + 8u * st,
+                      64 * hh, (j + (i ? kvb1 : 0)) * C::kBN, h, b);
+      }
+      __syncwarp();
+      issued = t + 1;
+    }
+  }
+  return issued;
+}
+
 template <int kStages>
 __device__ __forceinline__ void drain_ring(uint32_t bar_full0, int issued) {
   for (int t = issued > kStages ? issued - kStages : 0; t < issued; ++t)
     mbar_wait_quiet(bar_full0 + 8u * (t % kStages), (t / kStages) & 1);
 }
 
-template <int HD, bool kCausal, bool kMerge>
+// kSplit (non-merge launches that would leave SMs idle with one query tile
+// per CTA): both query-tile slots of a CTA work on the same tile, slot 0 on
+// the first half of its KV tiles and slot 1 on the second half; the two
+// partial results are merged in the epilogue.
+template <int HD, bool kCausal, bool kMerge, bool kSplit = false>
 __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_constant__ Flash2Params p) {
   using C = Cfg<HD>;
   constexpr int kD = C::kD;
@@ -289,9 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     bh = lin / p.n_cta_m;
   }
   const int qt0 = cta_m * p.tiles_per_cta;
-  const bool has_q1 = (p.tiles_per_cta == 2) && (qt0 + 1 < p.n_qtiles);
-  const int nkv0 = kv_tiles_for<kBN>(p, kCausal, qt0 * kBM);
-  const int nkv1 = has_q1 ? kv_tiles_for<kBN>(p, kCausal, (qt0 + 1) * kBM) : 0;
+  // split: slot 0 takes the first ceil(n/2) of the tile's n KV tiles, slot 1 the rest
+  const int nkv_split = kSplit ? kv_tiles_for<kBN>(p, kCausal, qt0 * kBM) : 0;
+  const bool has_q1 = kSplit ? (nkv_split > 1) : ((p.tiles_per_cta == 2) && (qt0 + 1 < p.n_qtiles));
+  const int nkv0 = kSplit ? (nkv_split + 1) / 2 : kv_tiles_for<kBN>(p, kCausal, qt0 * kBM);
+  const int nkv1 = kSplit ? nkv_split - nkv0
+                          : (has_q1 ? kv_tiles_for<kBN>(p, kCausal, (qt0 + 1) * kBM) : 0);
+  const int kvb1 = kSplit ? nkv0 : 0;  // first KV tile of slot 1
   const int nkv = nkv0 > nkv1 ? nkv0 : nkv1;
 
   // ---- setup ----
@@ -336,19 +374,22 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_k);
-      mbar_arrive_expect_tx(bar_q, (has_q1 ? 2 : 1) * kQTileBytes);
+      mbar_arrive_expect_tx(bar_q, ((has_q1 && !kSplit) ? 2 : 1) * kQTileBytes);
 #pragma unroll
       for (int hh = 0; hh < C::kHalves; ++hh) {
         tma_load_4d(s_q[0] + hh * (kBM * 128), &p.tm_q, bar_q, 64 * hh, qt0 * kBM, bh % p.nh,
                     bh / p.nh);
-        if (has_q1)
+        if (has_q1 && !kSplit)
           tma_load_4d(s_q[1] + hh * (kBM * 128), &p.tm_q, bar_q, 64 * hh, (qt0 + 1) * kBM,
                       bh % p.nh, bh / p.nh);
       }
     }
     __syncwarp();
-    const int issued = produce_ring<HD, kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv,
-                                              bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
+    const int issued =
+        kSplit ? produce_ring_split<HD, kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv0, nkv1, kvb1,
+                                                  bh % p.nh, bh / p.nh, lane, abort_flag, p.err)
+               : produce_ring<HD, kStagesK>(&p.tm_k, s_k0, bar_kfull0, bar_kempty0, nkv, bh % p.nh,
+                                            bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) {
       // Drain: let every copy this CTA started land before shared memory is released.
       mbar_wait_quiet(bar_q, 0);
@@ -357,8 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
   } else if (warp == 2) {
     // ======================= V producer =======================
     if (lane == 0) tma_prefetch_desc(&p.tm_v);
-    const int issued = produce_ring<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv,
-                                              bh % p.nh, bh / p.nh, lane, abort_flag, p.err);
+    const int issued =
+        kSplit ? produce_ring_split<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv0, nkv1, kvb1,
+                                                  bh % p.nh, bh / p.nh, lane, abort_flag, p.err)
+               : produce_ring<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv, bh % p.nh,
+                                            bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
@@ -380,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     constexpr uint64_t kQHalfEnc = (kBM * 128) >> 4;      // Q half block
     constexpr uint64_t kKHalfEnc = (kBN * 128) >> 4;      // K half block
     auto issue_s = [&](int i, int st) {
-      const uint64_t a = i ? dq1 : dq0;
+      const uint64_t a = (i && !kSplit) ? dq1 : dq0;
       const uint64_t b = dk0 + static_cast<uint64_t>(st) * kStageEnc;
       const uint32_t d = tm + col_s(i);
       if (elect_one()) {
@@ -410,52 +454,66 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       __syncwarp();
     };
 
+    // Ring index of slot i's KV step j: j, or 2j + i when the two slots
+    // stream different KV tiles through one ring (split).
+    auto ring = [&](int i, int j) { return kSplit ? 2 * j + i : j; };
     bool ok = warp_wait_issuer(bar_q, 0, abort_flag, p.err);
     if (ok && nkv > 0) ok = warp_wait_issuer(bar_kfull(0), 0, abort_flag, p.err);
+    if (ok && kSplit && nkv1 > 0) ok = warp_wait_issuer(bar_kfull(1), 0, abort_flag, p.err);
     if (ok && nkv > 0) {
       tc_fence_after();
       if (nkv0 > 0) issue_s(0, 0);
-      if (nkv1 > 0) issue_s(1, 0);
-      commit_to(bar_kempty(0));
+      if (kSplit) commit_to(bar_kempty(0));
+      if (nkv1 > 0) issue_s(1, ring(1, 0));
+      if (!kSplit || nkv1 > 0) commit_to(bar_kempty(ring(1, 0)));
       // Issue order per iteration j, matching the staggered softmax tiles
       // (tile 1 runs about half a KV step behind tile 0): S_0(j+1),
       // P_1(j-1) V, S_1(j+1), P_0(j) V. Each MMA waits only for its own
       // inputs, so neither tile's softmax waits behind the other's.
       for (int j = 0; j <= nkv; ++j) {
         const bool s_next = j + 1 < nkv;
-        const int sk = (j + 1) % kStagesK;
+        const int rk0 = ring(0, j + 1);
+        const int sk = rk0 % kStagesK;
         if (s_next) {
-          if (!warp_wait_issuer(bar_kfull(sk), ((j + 1) / kStagesK) & 1, abort_flag, p.err)) break;
+          if (!warp_wait_issuer(bar_kfull(sk), (rk0 / kStagesK) & 1, abort_flag, p.err)) break;
           if (lane == 0) FL_TRACE_EV(10, j);
         }
         if (j + 1 < nkv0) {
           if (!warp_wait_issuer(bar_sfree(0), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
           issue_s(0, sk);
+          if (kSplit) commit_to(bar_kempty(sk));  // that K tile is read by S_0 only
           if (lane == 0) FL_TRACE_EV(12, j);
         }
         if (j >= 1) {
           // P_1 V of the previous KV tile, then that V stage is free.
-          const int sv = (j - 1) % kStagesV;
+          const int rv1 = ring(1, j - 1);
+          const int sv = rv1 % kStagesV;
           if (j - 1 < nkv1) {
+            // (split: slot 1's V tile is its own ring entry, not yet waited for)
+            if (kSplit && !warp_wait_issuer(bar_vfull(sv), (rv1 / kStagesV) & 1, abort_flag, p.err)) break;
             if (!warp_wait_issuer(bar_p(1), (j - 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
             if (lane == 0) FL_TRACE_EV(9, j - 1);
             issue_pv(1, sv, j - 1);
             if (lane == 0) FL_TRACE_EV(13, j - 1);
           }
-          commit_to(bar_vempty(sv));
+          if (!kSplit || j - 1 < nkv1) commit_to(bar_vempty(sv));
         }
+        const int rk1 = ring(1, j + 1);
+        const int sk1 = rk1 % kStagesK;
         if (j + 1 < nkv1) {
+          if (kSplit && !warp_wait_issuer(bar_kfull(sk1), (rk1 / kStagesK) & 1, abort_flag, p.err)) break;
           if (!warp_wait_issuer(bar_sfree(1), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
-          issue_s(1, sk);
+          issue_s(1, sk1);
         }
-        if (s_next) commit_to(bar_kempty(sk));
+        if (kSplit ? (j + 1 < nkv1) : s_next) commit_to(bar_kempty(sk1));
         if (j < nkv) {
           // V_j must be resident for P_0 V (and later P_1 V).
-          const int sv = j % kStagesV;
-          if (!warp_wait_issuer(bar_vfull(sv), (j / kStagesV) & 1, abort_flag, p.err)) break;
+          const int rv0 = ring(0, j);
+          const int sv = rv0 % kStagesV;
+          if (!warp_wait_issuer(bar_vfull(sv), (rv0 / kStagesV) & 1, abort_flag, p.err)) break;
           if (j < nkv0) {
             if (!warp_wait_issuer(bar_p(0), j & 1, abort_flag, p.err)) break;
             tc_fence_after();
@@ -463,6 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
             issue_pv(0, sv, j);
             if (lane == 0) FL_TRACE_EV(11, j);
           }
+          if (kSplit) commit_to(bar_vempty(sv));  // that V tile is read by P_0 V only
         }
       }
     }
@@ -484,8 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     const uint32_t tS = tmem + lane_base + col_s(i);
     const uint32_t tP = tmem + lane_base + col_p(i);
     const uint32_t tO = tmem + lane_base + col_o(i);
-    const int q_start = (qt0 + i) * kBM;
+    const int q_start = (qt0 + (kSplit ? 0 : i)) * kBM;
     const int my_nkv = (i == 0) ? nkv0 : nkv1;
+    const int kv_base = (i == 0) ? 0 : kvb1;  // first KV tile of this slot
     const bool active = (i == 0) || has_q1;
 
     float sc = p.scale_log2;
@@ -524,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         for (int c = 0; c < kBN; ++c) s[c] *= sc;
         scl = 1.0f;
       }
-      const int k_start = j * kBN;
+      const int k_start = (j + kv_base) * kBN;
       // keys visible to this row: c < limit
       long long lim = p.nk - k_start;
       if (kCausal) {
@@ -655,11 +715,42 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         for (int c = 0; c < 32; ++c) o[32 * h + c] = tmp[c];
       }
     }
+    if constexpr (kSplit) {
+      // Slot 1 hands its row (max, sum) to slot 0 through its unused Q
+      // buffer; slot 0 reads slot 1's O from TMEM (same lanes) and merges:
+      // O = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)).
+      float2* xch = reinterpret_cast<float2*>(smem + kSmemQ + kQTileBytes);
+      if (i == 1) xch[t] = make_float2(do_out ? m_ref : -INFINITY, do_out ? l : 0.0f);
+      named_bar_sync(3, 256);
+      if (i == 0 && do_out) {
+        const float2 ml1 = xch[t];
+        const float m = fmaxf(m_ref, ml1.x);
+        const float w0 = (m_ref == -INFINITY) ? 0.0f : ex2_approx(m_ref - m);
+        const float w1 = (ml1.x == -INFINITY) ? 0.0f : ex2_approx(ml1.x - m);
+        l = l * w0 + ml1.y * w1;
+        m_ref = m;
+        if (__any_sync(0xffffffffu, ml1.x != -INFINITY)) {
+          uint32_t tmp[32];
+#pragma unroll
+          for (int h = 0; h < kD / 32; ++h) {
+            tmem_ld32_wait(tmem + lane_base + col_o(1) + h * 32, tmp);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              o[32 * h + c] = __float_as_uint(fmaf(__uint_as_float(o[32 * h + c]), w0,
+                                                   __uint_as_float(tmp[c]) * w1));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < kD; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * w0);
+        }
+      }
+    }
     const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
     if (!kMerge) {
       // A tile whose rows see no key at all (key positions offset past the
-      // queries) is written as zeros, as fully masked rows are.
-      const bool write = active && ok;
+      // queries) is written as zeros, as fully masked rows are. (Split:
+      // slot 0 writes the merged tile.)
+      const bool write = active && ok && !(kSplit && i == 1);
       if (write && !do_out) {
         // The staging buffer is this tile's Q buffer: let its load land first
         // (with no KV step nothing else waited for it).
@@ -795,10 +886,14 @@ bool encode_rows_map(CUtensorMap* tm, const void* base, int64_t rows, int64_t H,
 
 namespace {
 
-template <int HD, bool kCausal, bool kMerge>
+#ifndef FL_SPLIT_KV
+#define FL_SPLIT_KV 1
+#endif
+
+template <int HD, bool kCausal, bool kMerge, bool kSplit = false>
 cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t stream) {
   constexpr int kSmemAlloc = Cfg<HD>::kSmemAlloc;
-  auto kern = flash2_fwd_kernel<HD, kCausal, kMerge>;
+  auto kern = flash2_fwd_kernel<HD, kCausal, kMerge, kSplit>;
   static int configured_mask = 0;  // bit per device (up to 32 devices)
   int dev = 0;
   cudaGetDevice(&dev);
@@ -852,6 +947,16 @@ cudaError_t launch_flash2(const void* q, const void* k, const void* v, void* o_f
   const int64_t grid = static_cast<int64_t>(prm.n_cta_m) * BH;
   if (grid <= 0 || grid > 0x7fffffff) return cudaErrorInvalidConfiguration;
   const int g = static_cast<int>(grid);
+  // One query tile per CTA leaves the second softmax warpgroup idle: give it
+  // the second half of the tile's KV tiles instead (split), when there are
+  // at least two.
+  if (FL_SPLIT_KV && !merge && prm.tiles_per_cta == 1 && prm.n_ktiles >= 2) {
+    if (head_dim == 128)
+      return causal ? launch_variant<128, true, false, true>(prm, g, stream)
+                    : launch_variant<128, false, false, true>(prm, g, stream);
+    return causal ? launch_variant<64, true, false, true>(prm, g, stream)
+                  : launch_variant<64, false, false, true>(prm, g, stream);
+  }
   if (head_dim == 128) {
     if (merge) {
       return causal ? launch_variant<128, true, true>(prm, g, stream)

@@ -3,8 +3,9 @@
 Tolerance (north star): max-abs <= 2e-3 and mean-abs <= 2e-4 against fp32
 softmax(QK^T*scale)V on the same seeded fp16 inputs. Cases: the reference's
 own test matrix (thebigblender/FlashLite tests/test_correctness.py:61-90),
-the BASELINE configs 1-3, both dispatch classes (one / two query tiles per
-CTA), ragged N, N smaller than a tile, the default and a negative scale, the
+the BASELINE configs 1-3, both dispatch classes (two query tiles per CTA, or
+one query tile whose KV range is split between the CTA's two softmax
+warpgroups), ragged N, N smaller than a tile, the default and a negative scale, the
 zero-allocation ``out=`` form, and calls straight through the C ABI.
 """
 import ctypes
@@ -70,6 +71,24 @@ def test_two_tiles_per_cta_dispatch(cuda, N, causal):
     # B*H large enough that two query tiles per CTA still fill 148 SMs,
     # with an odd number of query tiles for N = 1100 / 2000 / 640.
     _run(cuda, 4, 16, N, causal, seed=5)
+
+
+@pytest.mark.parametrize("N", [384, 640, 1000, 2049])
+@pytest.mark.parametrize("causal", [False, True])
+def test_split_kv_one_tile_per_cta(cuda, N, causal):
+    # Few (b,h) slices, so one query tile per CTA: its KV tiles are split
+    # between the two softmax warpgroups (odd and even tile counts, ragged
+    # keys, causal tiles whose second half is empty) and merged in the
+    # epilogue; repeated calls give the same bits.
+    q, k, v = orc.make_qkv(1, 2, N, 64, seed=N + 7)
+    ref = orc.attention_fp32(q, k, v, 0.125, causal)
+    qd, kd, vd = (t.to(cuda) for t in (q, k, v))
+    a = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+    b = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+    torch.cuda.synchronize()
+    assert fa.device_error() == 0
+    assert torch.equal(a, b)
+    _check(a.cpu(), ref, f"split N{N} causal={causal}")
 
 
 @pytest.mark.parametrize("B,H,N,causal", [
