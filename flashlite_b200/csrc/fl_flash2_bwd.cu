@@ -11,14 +11,15 @@
 //    the CTA streams every query tile that sees them (causal: from the
 //    diagonal tile on) through a 2-deep TMA ring of (Q, dO, LSE, Delta).
 //  * everything is computed key-major, so TMEM lanes are the CTA's keys:
-//    S^T = K Q^T and dP^T = V dO^T land in TMEM (128 columns each); two
-//    gradient warpgroups (one thread per key, each taking 64 of the 128
+//    S^T = K Q^T and dP^T = V dO^T land in TMEM (128 columns each); four
+//    gradient warpgroups (one thread per key, each taking 32 of the 128
 //    query columns: P needs no row reduction since LSE is known) turn them
-//    into P^T and dS^T 32 columns at a time, write both back into columns
+//    into P^T and dS^T 16 columns at a time, write both back into columns
 //    the same warp has already read (fp16 pairs, operand A of the next MMAs:
-//    the queries of half h sit at columns 64 h .. 64 h + 31), and write dS^T
+//    queries 32c .. 32c + 31 sit at columns 32c .. 32c + 15), and write dS^T
 //    to shared memory in the MN-major layout that makes it dS, operand A of
-//    dQ = dS K.
+//    dQ = dS K. Four such warps per SM sub-partition hide each other's TMEM
+//    and MUFU latency.
 //  * the MMA warp then issues dV += P^T dO and dK += dS^T Q (A from TMEM,
 //    accumulated over the query tiles in TMEM) and dQ_i = dS K (A and B
 //    from shared memory, K read as MN-major B).
@@ -45,7 +46,7 @@ namespace {
 constexpr int kBM = 128;                  // query rows per tile
 constexpr int kBK = 128;                  // keys per CTA
 constexpr int kD = 64;                    // head dimension
-constexpr int kThreads = 512;             // producer/MMA | gradient x 2 | dQ drain
+constexpr int kThreads = 768;             // producer/MMA | gradient x 4 | dQ drain
 constexpr int kTile = 128 * kD * 2;       // 16 KB: one 128 x 64 fp16 tile
 constexpr int kStages = 2;                // (Q, dO, LSE, Delta) ring depth
 constexpr uint32_t kTmemCols = 512;
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     }
     for (int hq = 0; hq < 2; ++hq) {
       mbar_init(bar_s(hq), 1);
-      mbar_init(bar_p(hq), 4);  // one arrival per gradient warp of that half
+      mbar_init(bar_p(hq), 8);  // one arrival per gradient warp of that half
     }
     mbar_init(bar_mm, 1);
     mbar_init(bar_dqfree, 4);  // one arrival per dQ warp
@@ -253,15 +254,15 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
         tc_fence_after();
         if (elect_one()) {
           // dV += P^T dO and dK += dS^T Q over this half's 64 queries: A from
-          // TMEM (16 queries = 8 columns per K step, half h at column 64 h),
-          // B MN-major (16 rows = 2048 B per K step)
+          // TMEM (16 queries = 8 columns per K step; queries 32c.. at column
+          // 32c), B MN-major (16 rows = 2048 B per K step)
 #pragma unroll
           for (int kk = 4 * hq; kk < 4 * hq + 4; ++kk)
-            umma_f16_ts(tm + kColDV, tm + kColS + 64 * hq + 8 * (kk & 3), d_domn0 + so + 128 * kk,
+            umma_f16_ts(tm + kColDV, tm + kColS + 32 * (kk >> 1) + 8 * (kk & 1), d_domn0 + so + 128 * kk,
                         idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 4 * hq; kk < 4 * hq + 4; ++kk)
-            umma_f16_ts(tm + kColDK, tm + kColDP + 64 * hq + 8 * (kk & 3), d_qmn0 + so + 128 * kk,
+            umma_f16_ts(tm + kColDK, tm + kColDP + 32 * (kk >> 1) + 8 * (kk & 1), d_qmn0 + so + 128 * kk,
                         idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
           // dV, dK of this tile done: Q, dO of the stage and the TMEM columns
           // of P^T, dS^T are free
@@ -294,9 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     commit_to(bar_final);
     if (lane == 0) mbar_wait_quiet(bar_final, 0);
     __syncwarp();
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < 20) {
     // ======================= gradient warpgroups (one thread per key) =======================
-    const int qh = (warp - 4) >> 2;           // query half: columns 64 qh .. 64 qh + 63
+    const int gq = (warp - 4) >> 2;           // query columns 32 gq .. 32 gq + 31
+    const int qh = gq >> 1;                   // query half
     const int k = 32 * (warp & 3) + lane;     // key row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const uint32_t tS = tmem + lane_base + kColS;
@@ -319,17 +321,18 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       const float* lse2 = reinterpret_cast<const float*>(smem + kSmemVec + st * 2 * kBM * 4);
       const uint32_t ds_row = ds_row0 + (it & 1) * (2 * kTile);  // dS buffer of this tile
       const float* dlt = lse2 + kBM;
+      const int c = gq;  // this warp's 32-query chunk, in two 16-query parts
 #pragma unroll 1
-      for (int c = 2 * qh; c < 2 * qh + 2; ++c) {
-        uint32_t sr[32], dpr[32];
-        tmem_ld32_nowait(tS + 32 * c, sr);
-        tmem_ld32_nowait(tDP + 32 * c, dpr);
-        tmem_wait_ld_dep(sr);
-        tmem_wait_ld_dep(dpr);
-        uint32_t pk_p[16], pk_ds[16];
+      for (int u = 0; u < 2; ++u) {
+        uint32_t sr[16], dpr[16];
+        tmem_ld16_nowait(tS + 32 * c + 16 * u, sr);
+        tmem_ld16_nowait(tDP + 32 * c + 16 * u, dpr);
+        tmem_wait_ld16_dep(sr);
+        tmem_wait_ld16_dep(dpr);
+        uint32_t pk_p[8], pk_ds[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int q0 = 32 * c + 2 * e;
+        for (int e = 0; e < 8; ++e) {
+          const int q0 = 32 * c + 16 * u + 2 * e;
           const float2 l2 = *reinterpret_cast<const float2*>(lse2 + q0);
           const float2 d2 = *reinterpret_cast<const float2*>(dlt + q0);
           const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])),
@@ -347,17 +350,17 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
           pk_p[e] = pack_f16x2(pp.x, pp.y);
           pk_ds[e] = pack_f16x2(ds.x, ds.y);
         }
-        // P^T and dS^T into columns this warp has read already: queries
-        // 32c.. at column 64 (c / 2) + 16 (c % 2)
-        tmem_st16(tS + 64 * (c >> 1) + 16 * (c & 1), pk_p);
-        tmem_st16(tDP + 64 * (c >> 1) + 16 * (c & 1), pk_ds);
-        // dS^T row k, queries 32c..32c+31: half c / 2, chunks 4 (c % 2) .. +3
+        // P^T and dS^T into columns this warp has read: queries 32c + 16u..
+        // at column 32c + 8u
+        tmem_st8(tS + 32 * c + 8 * u, pk_p);
+        tmem_st8(tDP + 32 * c + 8 * u, pk_ds);
+        // dS^T row k, queries 32c + 16u ..: half c / 2, chunks 4 (c % 2) + 2u, +1
         const uint32_t half = ds_row + (c >> 1) * (kTile);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int ch = 4 * (c & 1) + u;
-          st_shared_v4(half + ((ch ^ (k & 7)) << 4), pk_ds[4 * u], pk_ds[4 * u + 1], pk_ds[4 * u + 2],
-                       pk_ds[4 * u + 3]);
+        for (int v = 0; v < 2; ++v) {
+          const int ch = 4 * (c & 1) + 2 * u + v;
+          st_shared_v4(half + ((ch ^ (k & 7)) << 4), pk_ds[4 * v], pk_ds[4 * v + 1], pk_ds[4 * v + 2],
+                       pk_ds[4 * v + 3]);
         }
       }
       tmem_st_wait();
@@ -366,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p(qh));
     }
-    // ---- dK, dV epilogue (query half 0 writes dV, half 1 dK) ----
+    // ---- dK, dV epilogue (warpgroups 0, 1 write dV, 2, 3 dK; 32 columns each) ----
     if (ok) ok = warp_wait(bar_final, 0, abort_flag, p.err);
     const int key = kv_start + k;
     if (ok && !*abort_flag) {
@@ -375,15 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
           (p.bnhd ? (static_cast<long long>(b) * p.n + key) * p.nh + h
                   : static_cast<long long>(bh) * p.n + key) * kD;
       {
-        const int which = qh;
-        uint32_t r[64];
-        const uint32_t col = tmem + lane_base + (which ? kColDK : kColDV);
-        tmem_ld64_wait(col, r);
+        const int which = gq >> 1;   // 0: dV, 1: dK
+        const int colh = gq & 1;     // columns 32 colh .. 32 colh + 31
+        uint32_t r[32];
+        const uint32_t col = tmem + lane_base + (which ? kColDK : kColDV) + 32 * colh;
+        tmem_ld32_wait(col, r);
         const float f = which ? p.scale : 1.0f;
         if (key < p.n) {
-          uint4* dst = reinterpret_cast<uint4*>((which ? p.dk : p.dv) + rowoff);
+          uint4* dst = reinterpret_cast<uint4*>((which ? p.dk : p.dv) + rowoff + 32 * colh);
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
+          for (int c = 0; c < 4; ++c)
             dst[c] = make_uint4(
                 pack_f16x2(__uint_as_float(r[8 * c + 0]) * f, __uint_as_float(r[8 * c + 1]) * f),
                 pack_f16x2(__uint_as_float(r[8 * c + 2]) * f, __uint_as_float(r[8 * c + 3]) * f),
@@ -392,9 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
         }
       }
     }
-  } else if (warp >= 12) {
+  } else if (warp >= 20) {
     // ======================= dQ drain (one thread per query row) =======================
-    const int t = threadIdx.x - 384;
+    const int t = threadIdx.x - 640;
     const uint32_t tQ = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + kColDQ;
     // staging: two [128 x 32] fp32 halves with the 128-byte swizzle of the
     // dQ tensor map (16-byte chunk c of row t at position c ^ (t % 8))
@@ -403,18 +407,22 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
     for (int it = 0; ok && it < nq; ++it) {
       if (!warp_wait(bar_mm, it & 1, abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
-      uint32_t r[64];
-      tmem_ld64_wait(tQ, r);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {  // 32 columns at a time
+        uint32_t r[32];
+        tmem_ld32_wait(tQ + 32 * hh, r);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const int c = 8 * hh + cc;
+          const float4 v = make_float4(__uint_as_float(r[4 * cc]) * p.scale, __uint_as_float(r[4 * cc + 1]) * p.scale,
+                                       __uint_as_float(r[4 * cc + 2]) * p.scale,
+                                       __uint_as_float(r[4 * cc + 3]) * p.scale);
+          *reinterpret_cast<float4*>(srow + (c >> 3) * (kBM * 128) + (((c & 7) ^ (t & 7)) << 4)) = v;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_dqfree);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float4 v = make_float4(__uint_as_float(r[4 * c]) * p.scale, __uint_as_float(r[4 * c + 1]) * p.scale,
-                                     __uint_as_float(r[4 * c + 2]) * p.scale,
-                                     __uint_as_float(r[4 * c + 3]) * p.scale);
-        *reinterpret_cast<float4*>(srow + (c >> 3) * (kBM * 128) + (((c & 7) ^ (t & 7)) << 4)) = v;
-      }
       fence_proxy_async_smem();
       named_bar_sync(1, 128);
       if (t == 0) {
