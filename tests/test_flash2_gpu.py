@@ -177,6 +177,30 @@ def test_out_buffer_zero_alloc(cuda):
     _check(out_buf.cpu(), orc.attention_fp32(q, k, v, 0.125, True), "out=")
 
 
+@pytest.mark.parametrize("B,H,N,causal", [(2, 8, 1024, False), (2, 8, 4096, True), (1, 2, 640, False)])
+def test_back_to_back_calls_see_previous_output(cuda, B, H, N, causal):
+    # Each launch lets the next kernel on the stream start its set-up early;
+    # a call that reads the previous call's output, issued without a
+    # synchronisation in between, must still see all of it.
+    q, k, v = orc.make_qkv(B, H, N, 64, seed=N + B)
+    qd, kd, vd = (t.to(cuda) for t in (q, k, v))
+    o1 = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+    o2 = fa.forward_flash2(o1, kd, vd, 0.125, causal)      # reads o1
+    o3 = fa.forward_flash2(qd, o2, vd, 0.125, causal)      # reads o2 as keys
+    torch.cuda.synchronize()
+    assert fa.device_error() == 0
+    r1 = fa.forward_flash2(qd, kd, vd, 0.125, causal)
+    torch.cuda.synchronize()
+    r2 = fa.forward_flash2(r1, kd, vd, 0.125, causal)
+    torch.cuda.synchronize()
+    r3 = fa.forward_flash2(qd, r2, vd, 0.125, causal)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, r1) and torch.equal(o2, r2) and torch.equal(o3, r3)
+    if N <= 1024:
+        ref2 = orc.attention_fp32(o1.cpu(), k, v, 0.125, causal)
+        _check(o2.cpu(), ref2, "chained")
+
+
 def test_deterministic(cuda):
     q, k, v = (t.to(cuda) for t in orc.make_qkv(2, 8, 1024, 64, seed=9))
     a = fa.forward_flash2(q, k, v, 0.125, False)
