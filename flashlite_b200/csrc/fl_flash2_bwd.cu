@@ -161,6 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_bwd_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: set-up above overlaps the preprocess
+  // kernel; its Delta / LSE rows (and the cleared dQ accumulator) are read
+  // only after this wait.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     // ======================= TMA producer =======================
@@ -452,6 +456,8 @@ __global__ void flash2_bwd_prep_kernel(const __half* __restrict__ o, const __hal
                                        const float* __restrict__ lse, float* __restrict__ lse2,
                                        float* __restrict__ delta, int n, int npad, long long rows,
                                        int nh, int bnhd) {
+  // the main kernel may start its set-up now (it waits for this grid's writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long row = gid >> 3;
   const int sub = threadIdx.x & 7;
@@ -512,8 +518,17 @@ cudaError_t launch_bwd_variant(const BwdParams& prm, int grid, cudaStream_t stre
     if (e != cudaSuccess) return e;
     configured_mask |= (1 << (dev & 31));
   }
-  kern<<<grid, kThreads, kSmemAlloc, stream>>>(prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, prm);
 }
 
 }  // namespace
