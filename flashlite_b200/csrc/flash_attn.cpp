@@ -62,8 +62,16 @@ torch::Tensor forward_flash2(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   if (out_tensor.numel() == 0) return out_tensor;
   const c10::cuda::CUDAGuard guard(q.device());
   // sm_scale == 0 -> 1/sqrt(D) is applied by the C ABI (csrc/kernel_flash2.cu:769-771)
-  check_status(fl_flash2_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_tensor.data_ptr(), B, H,
-                             N, D, static_cast<float>(sm_scale), is_causal ? 1 : 0, stream_of(q)));
+  void* const stream = stream_of(q);
+  int status;
+  {
+    // The launch blocks while the device's launch queue is full; other
+    // Python threads keep running meanwhile (the error text is thread-local).
+    pybind11::gil_scoped_release no_gil;
+    status = fl_flash2_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_tensor.data_ptr(), B, H, N,
+                           D, static_cast<float>(sm_scale), is_causal ? 1 : 0, stream);
+  }
+  check_status(status);
   return out_tensor;
 }
 

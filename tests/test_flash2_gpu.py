@@ -273,3 +273,34 @@ def test_config4_sampled_rows(cuda):
     rows = torch.tensor([0, 1, 127, 128, 4095, 4096, 8000, 8191])
     ref = orc.attention_rows_fp32(q.view(S, N, 64), k.view(S, N, 64), v.view(S, N, 64), rows, 0.125, True)
     _check(out.view(S, N, 64)[:, rows], ref, "config4 rows")
+
+
+def test_concurrent_python_threads(cuda):
+    # the binding releases the GIL around the launch: calls from several
+    # threads, each on its own stream, give the single-thread result
+    import threading
+
+    q, k, v = (t.to(cuda) for t in orc.make_qkv(2, 8, 1024, 64, seed=31))
+    ref = fa.forward_flash2(q, k, v, 0.0, True)
+    torch.cuda.synchronize()
+    results, errors = [None] * 4, []
+
+    def work(i):
+        try:
+            s = torch.cuda.Stream(cuda)
+            with torch.cuda.stream(s):
+                outs = [fa.forward_flash2(q, k, v, 0.0, True) for _ in range(50)]
+            s.synchronize()
+            results[i] = outs[-1]
+        except Exception as e:  # surfaced in the main thread below
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    assert fa.device_error() == 0
+    for r in results:
+        assert torch.equal(r, ref)
