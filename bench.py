@@ -1,29 +1,42 @@
 """Benchmark of the FA2 forward hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg3|cfg3c|cfg2|cfg2c|cfg4|cfg5|bwd3|bwd3c|d128_3|d128_3c]
-
-(bwd3/bwd3c: the backward pass, d128_3/d128_3c: the head_dim-128 forward, on
-the config-3 shape; extensions without a reference counterpart.)
+                    [--workload cfg3|cfg3c|cfg2|cfg2c|cfg1|cfg4|cfg5|bwd3|bwd3c|d128_3|d128_3c]
+                    [--no-legs] [--no-cpu-baseline] [--ring-layout contiguous|zigzag]
 
 Metric: FA2 forward TFLOP/s per B200 (fp16, D=64), FLOPs =
 4·B·H·N²·D halved for causal (reference benchmarks/benchmark_throughput.py:23-31).
 A step is one forward_flash2 call over one batch. The default workload is
 BASELINE config 3 (B=2, H=8, N=4096, D=64, non-causal: the headline). With N
 GPUs (torchrun) every rank runs its own config-3 batch of (b,h) slices of a
-global B=2·N problem (head sharding, no communication): weak scaling.
+global B=2·N problem (head sharding, no communication): weak scaling, so the
+N=1 line is the single-GPU headline.
 
-Timing: W untimed warm-up steps, then K steps between CUDA events on the
-launching stream, bracketed by a barrier and a device synchronize; the max
-over ranks is reported. Steps rotate through enough independent input sets
-that their total footprint is over 3x the 126 MB L2, so every step reads its
-inputs from HBM. ``e2e`` repeats the measurement through the public API with
-the inputs copied from pinned host memory and the output read back each step.
+Timing of ``value``: W untimed warm-up steps, then K steps between CUDA events
+on the launching stream, bracketed by a barrier and a device synchronize; the
+max over ranks is reported. Steps rotate through enough independent input
+sets that their total footprint is over 3x the 126 MB L2, so every step reads
+its inputs from HBM. Beside it: ``median`` (median of per-call CUDA-event
+times), ``same_method`` (the reference benchmark's own method: median of 100
+after 25 warm-up on one input set, benchmarks/benchmark_throughput.py:34-54),
+``e2e`` (the step through the public API with inputs copied from pinned host
+memory and the output read back), ``naive`` (forward_naive, timed as the
+reference benchmark does, :125-136), ``peak_mem_mb`` (peak allocated memory of
+forward_flash2 with and without ``out=`` against unfused torch attention,
+:170-197) and ``cfg1``.
+
+Multi-GPU legs (``cfg4``, ``cfg5`` sub-objects, at every N, on by default for
+the config-3 workloads): config 4 (B16 H32 N8192 causal, 512 slices split
+over the ranks: strong scaling) and config 5 (B1 H8 N131072 causal, sequence
+sharded, NCCL ring, contiguous and zig-zag layouts). Each leg times its step,
+the same problem on one GPU (rank 0 alone, for the efficiency), and checks
+sampled output rows of every rank against the CPU fp32 oracle.
 
 ``--impl reference`` runs the reference's CPU math path (torch fp32
-matmul-softmax-matmul on all host threads, the oracle port) on a bounded
-sample of the same workload, and, when a GPU and the reference kernels built
-from its own sources (oracle/_ref) are present, also times those kernels.
+matmul-softmax-matmul on all host threads, the oracle port) on the same
+workload and, when a GPU and the reference kernels built from its own sources
+(oracle/_ref) are present, also times those kernels and PyTorch SDPA. That
+process loads no code of this package.
 """
 from __future__ import annotations
 
@@ -31,7 +44,6 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -43,9 +55,12 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 L2_BYTES = 126 * 1024 * 1024
+D = 64
+TOL_MAX, TOL_MEAN = 2e-3, 2e-4  # north-star tolerance against the fp32 oracle
 
 WORKLOADS = {
     # name: (B, H, N, causal, description)
+    "cfg1": (1, 2, 128, False, "BASELINE config 1: B1 H2 N128 D64 non-causal"),
     "cfg2": (2, 8, 1024, False, "BASELINE config 2: B2 H8 N1024 D64 non-causal"),
     "cfg2c": (2, 8, 1024, True, "BASELINE config 2: B2 H8 N1024 D64 causal"),
     "cfg3": (2, 8, 4096, False, "BASELINE config 3: B2 H8 N4096 D64 non-causal (headline)"),
@@ -64,8 +79,13 @@ EXT_WORKLOADS = {
 }
 
 
-def flops(B, H, N, D, causal):
-    return (2.0 if causal else 4.0) * B * H * N * N * D
+def flops(B, H, N, D_, causal):
+    return (2.0 if causal else 4.0) * B * H * N * N * D_
+
+
+def median(xs):
+    s = sorted(xs)
+    return s[len(s) // 2]
 
 
 # ----------------------------------------------------------------------------
@@ -101,19 +121,32 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
 # ----------------------------------------------------------------------------
 # clocks during the timed region
 # ----------------------------------------------------------------------------
 class ClockSampler:
-    """Polls SM clock and throttle reasons through NVML in a thread."""
+    """Polls SM clock and throttle reasons through NVML in a thread.
+
+    ``mark()`` splits the samples taken so far (the timed region) from those
+    of an untimed sustained pass of the same step that follows it, so a short
+    timed region still gets a clock reading."""
 
     REASONS = {
         "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
         "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, index: int, period_s: float = 0.002):
+    def __init__(self, index: int, period_s: float = 0.0005):
         self.samples, self.reasons = [], set()
+        self.n_timed = None
         self.max_mhz = None
         self._stop = threading.Event()
         self._t = None
@@ -150,6 +183,9 @@ class ClockSampler:
             self._t.start()
         return self
 
+    def mark(self):
+        self.n_timed = len(self.samples)
+
     def __exit__(self, *exc):
         self._stop.set()
         if self._t is not None:
@@ -163,9 +199,11 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        s = sorted(self.samples)
-        return {"sm_mhz": s[len(s) // 2], "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(s)}
+        return {"sm_mhz": median(self.samples), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(self.samples), "reasons": sorted(self.reasons),
+                "samples": len(self.samples),
+                "samples_timed_region": self.n_timed if self.n_timed is not None else len(self.samples),
+                "window": "timed region plus an untimed sustained pass of the same step right after it"}
 
 
 def measured_peaks():
@@ -192,27 +230,347 @@ def profiled_traffic(kernel: str, workload: str):
 
 
 # ----------------------------------------------------------------------------
-# our arm
+# seeded synthetic inputs, generated on the device
 # ----------------------------------------------------------------------------
+def dev_slices(idx, N, seed, device, scale=1.0):
+    """q, k, v [len(idx), N, D] fp16: i.i.d. N(0,1)·scale, each (b,h) slice
+    (and tensor) from its own CUDA generator, so values do not depend on how
+    slices are sharded over ranks."""
+    g = torch.Generator(device=device)
+    out = []
+    for name in range(3):
+        t = torch.empty(len(idx), N, D, dtype=torch.float16, device=device)
+        for r, s in enumerate(idx):
+            g.manual_seed((seed * 1_000_003 + s) * 4 + name)
+            t[r] = torch.randn(N, D, generator=g, device=device) * scale
+        out.append(t)
+    return out
+
+
+RING_BLOCK = 1024  # rows per generator block of the sequence-sharded inputs
+
+
+def dev_rows(row0, nrows, H, seed, device, scale, heads=None):
+    """q, k, v [1, len(heads), nrows, D] fp16 for global rows [row0, row0+nrows)
+    of a [1, H, N, D] problem: each (1024-row block, head, tensor) draws from
+    its own CUDA generator, so any rank can produce any rows."""
+    assert row0 % RING_BLOCK == 0 and nrows % RING_BLOCK == 0
+    heads = list(range(H)) if heads is None else heads
+    g = torch.Generator(device=device)
+    out = []
+    for name in range(3):
+        t = torch.empty(1, len(heads), nrows, D, dtype=torch.float16, device=device)
+        for hi, h in enumerate(heads):
+            for b in range(nrows // RING_BLOCK):
+                blk = row0 // RING_BLOCK + b
+                g.manual_seed((seed * 1_000_003 + blk * H + h) * 4 + name)
+                t[0, hi, b * RING_BLOCK:(b + 1) * RING_BLOCK] = \
+                    torch.randn(RING_BLOCK, D, generator=g, device=device) * scale
+        out.append(t)
+    return out
+
+
 def rank_slices(workload, world, rank):
+    from flashlite_b200.parallel_attn import shard_range
+
     B, H, N, causal, _ = WORKLOADS[workload]
     if workload == "cfg4":  # strong scaling: fixed 512 slices split over ranks
-        total = B * H
-        assert total % world == 0
-        per = total // world
-        return range(rank * per, (rank + 1) * per), total, N, causal, "strong"
+        return shard_range(B * H, world, rank), B * H, N, causal, "strong"
     per = B * H  # weak scaling: each rank owns one config-sized batch
     return range(rank * per, (rank + 1) * per), per * world, N, causal, "weak"
 
 
-def make_inputs(slices, N, seed, device=None):
-    from oracle.attention_oracle import make_qkv  # seeded host generator (shared with tests)
-
-    q, k, v = make_qkv(1, len(slices), N, 64, seed=seed, slices=slices)
-    shape = (1, len(slices), N, 64)
-    return q.view(shape), k.view(shape), v.view(shape)
+def l2_flush_buffer(device):
+    return torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
 
 
+def time_steps_flushed(step, steps, warmup, flush, stream):
+    """Per-step CUDA-event times (ms), each step preceded by an untimed write
+    of a buffer larger than L2."""
+    for _ in range(warmup):
+        step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def median_ms_ref_method(fn, warm=25, runs=100):
+    """benchmarks/benchmark_throughput.py:34-54: median of `runs` CUDA-event
+    timings after `warm` calls (inputs stay in L2 between calls)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
+    for a, b in es:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return median([a.elapsed_time(b) for a, b in es])
+
+
+# ----------------------------------------------------------------------------
+# parity of sampled rows against the CPU fp32 oracle (the checker)
+# ----------------------------------------------------------------------------
+def row_errors(out_rows, q_all, k_all, v_all, rows, sm_scale, causal):
+    """(max-abs, sum-abs, count) of out_rows [S, R, D] against the oracle's
+    rows of q_all/k_all/v_all [S, N, D] (host or device tensors)."""
+    from oracle.attention_oracle import attention_rows_fp32
+
+    ref = attention_rows_fp32(q_all.cpu(), k_all.cpu(), v_all.cpu(), rows, sm_scale, causal)
+    err = (out_rows.float().cpu() - ref).abs()
+    return float(err.max()), float(err.sum()), err.numel()
+
+
+def reduce_errors(errs, world, device):
+    mx = max_over_ranks(max(e[0] for e in errs), world, device)
+    tot = sum_over_ranks(sum(e[1] for e in errs), world, device)
+    cnt = sum_over_ranks(float(sum(e[2] for e in errs)), world, device)
+    mean = tot / max(cnt, 1.0)
+    return {"max_abs": mx, "mean_abs": mean, "values_checked": int(cnt),
+            "ok": bool(mx <= TOL_MAX and mean <= TOL_MEAN), "tolerance": [TOL_MAX, TOL_MEAN]}
+
+
+# ----------------------------------------------------------------------------
+# multi-GPU legs: config 4 (head sharded) and config 5 (ring)
+# ----------------------------------------------------------------------------
+def leg_cfg4(world, rank, device, steps, warmup, flush, stream):
+    """512 (b,h) slices of N=8192 causal split over ranks."""
+    from flashlite_b200 import flash_attn_wmma as fa
+    from flashlite_b200.parallel_attn import shard_range
+
+    B, H, N, causal, desc = WORKLOADS["cfg4"]
+    total, scale, seed = B * H, 0.125, 4
+
+    def run_on(idx):
+        q, k, v = dev_slices(idx, N, seed, device)
+        shape = (1, len(idx), N, D)
+        q, k, v = (t.view(shape) for t in (q, k, v))
+        o = torch.empty_like(q)
+        ts = time_steps_flushed(lambda: fa.forward_flash2(q, k, v, scale, causal, out=o),
+                                steps, warmup, flush, stream)
+        return q, k, v, o, ts
+
+    mine = shard_range(total, world, rank)
+    q, k, v, o, ts = run_on(mine)
+    ms = max_over_ranks(median(ts), world, device)
+    # parity: first and last slice of this rank, rows spread over the sequence
+    rows = torch.tensor([0, 1, 127, 128, N // 2 - 1, N // 2, N - 129, N - 1])
+    errs = []
+    for i in (0, len(mine) - 1):
+        errs.append(row_errors(o[0, i][rows][None], q[0, i][None], k[0, i][None], v[0, i][None],
+                               rows, scale, causal))
+    parity = reduce_errors(errs, world, device)
+    del q, k, v, o
+    # the same problem on one GPU (rank 0 alone), for the efficiency
+    barrier(world, device)
+    t1 = None
+    if world == 1:
+        t1 = ms
+    elif rank == 0:
+        *_, ts1 = run_on(range(total))
+        t1 = median(ts1)
+    barrier(world, device)
+    torch.cuda.empty_cache()
+    f = flops(B, H, N, D, causal)
+    res = {"workload": desc, "scaling": "strong", "slices_per_rank": len(mine),
+           "ms_per_step": round(ms, 4), "tflops": round(f / (ms * 1e-3) / 1e12, 2),
+           "timing": f"median of {steps} steps after {warmup} warm-up, L2 flushed between steps, max over ranks",
+           "parity": parity}
+    if rank == 0:
+        res["one_gpu_ms"] = round(t1, 4)
+        res["efficiency"] = round(t1 / (world * ms), 4)
+    return res
+
+
+def ring_inputs(world, rank, layout, N, H, seed, scale, device):
+    """This rank's q, k, v and the global query rows each local row holds."""
+    if layout == "zigzag" and world > 1:
+        from flashlite_b200.parallel_attn import zigzag_chunks
+
+        c = N // (2 * world)
+        parts = [dev_rows(ch * c, c, H, seed, device, scale) for ch in zigzag_chunks(rank, world)]
+        q, k, v = (torch.stack([parts[0][i], parts[1][i]]) for i in range(3))
+        starts = [ch * c for ch in zigzag_chunks(rank, world)]
+        return q, k, v, starts, c
+    nb = N // world
+    q, k, v = dev_rows(rank * nb, nb, H, seed, device, scale)
+    return q, k, v, [rank * nb], nb
+
+
+def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
+    """B1 H8 N131072 causal, sequence sharded over ranks."""
+    from flashlite_b200 import flash_attn_wmma as fa
+    from flashlite_b200.parallel_attn import RingAttention, ZigzagRingAttention
+
+    B, H, N, causal, desc = WORKLOADS["cfg5"]
+    scale, seed, sm_scale = 0.5, 5, 0.125
+    q, k, v, starts, rows_per_part = ring_inputs(world, rank, layout, N, H, seed, scale, device)
+    out = torch.empty_like(q)
+    o_acc = torch.empty(q.shape, dtype=torch.float32, device=device)
+    lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=device)
+    ring = None
+    if world > 1:
+        ring = ZigzagRingAttention() if layout == "zigzag" else RingAttention()
+
+    def step(events=None):
+        if ring is None:
+            fa.forward_flash2(q, k, v, sm_scale, causal, out=out)
+        else:
+            ring.forward(q, k, v, sm_scale, causal, out=out, o_acc=o_acc, lse=lse, events=events)
+
+    ts = time_steps_flushed(step, steps, warmup, flush, stream)
+    ms = max_over_ranks(median(ts), world, device)
+    breakdown = None
+    if ring is not None:
+        # one instrumented step: block compute vs exchange wait per ring step
+        flush.zero_()
+        evs = []
+        step(evs)
+        torch.cuda.synchronize()
+        comp = sum(e[0].elapsed_time(e[1]) for e in evs)
+        wait = sum(e[1].elapsed_time(e[2]) for e in evs)
+        breakdown = {"compute_ms_max": round(max_over_ranks(comp, world, device), 4),
+                     "compute_ms_min": round(-max_over_ranks(-comp, world, device), 4),
+                     "exposed_exchange_ms_max": round(max_over_ranks(wait, world, device), 4)}
+        c_max, c_min = breakdown["compute_ms_max"], breakdown["compute_ms_min"]
+        if breakdown["exposed_exchange_ms_max"] > 0.1 * ms:
+            limit = "K/V exchange not hidden behind the block compute"
+        elif c_max > 1.15 * c_min:
+            limit = ("causal load imbalance: the rank holding the last rows computes "
+                     f"{c_max / max(c_min, 1e-9):.2f}x the lightest rank's blocks")
+        else:
+            limit = "block compute (the ring's per-step kernel launches on N/P-row blocks)"
+        breakdown["limiting_step"] = limit
+    # parity: sampled rows of this rank (first and last rows of each part) on
+    # the first and last head, against the oracle over the whole causal prefix
+    errs = []
+    for hh in (0, H - 1):
+        last = max(starts) + rows_per_part
+        kq, kk, kv = dev_rows(0, last, H, seed, device, scale, heads=[hh])
+        for pi, st in enumerate(starts):
+            loc = torch.tensor([0, rows_per_part // 2, rows_per_part - 1])
+            glob = loc + st
+            got = (out[pi, 0, hh] if q.dim() == 5 else out[0, hh])[loc]
+            errs.append(row_errors(got[None], kq[0, 0][None], kk[0, 0][None], kv[0, 0][None],
+                                   glob, sm_scale, causal))
+        del kq, kk, kv
+    parity = reduce_errors(errs, world, device)
+    del q, k, v, out, o_acc, lse
+    if ring is not None:
+        del ring
+    barrier(world, device)
+    t1 = None
+    if world == 1:
+        t1 = ms
+    elif rank == 0:
+        qa, ka, va = dev_rows(0, N, H, seed, device, scale)
+        oa = torch.empty_like(qa)
+        t1 = median(time_steps_flushed(lambda: fa.forward_flash2(qa, ka, va, sm_scale, causal, out=oa),
+                                       steps, warmup, flush, stream))
+        del qa, ka, va, oa
+    barrier(world, device)
+    torch.cuda.empty_cache()
+    f = flops(B, H, N, D, causal)
+    res = {"workload": desc, "scaling": "strong",
+           "layout": (layout if world > 1 else "single GPU"),
+           "ms_per_step": round(ms, 4), "tflops": round(f / (ms * 1e-3) / 1e12, 2),
+           "timing": f"median of {steps} steps after {warmup} warm-up, L2 flushed between steps, max over ranks",
+           "parity": parity}
+    if breakdown is not None:
+        res["breakdown"] = breakdown
+    if layout == "contiguous" and world > 1:
+        res["causal_speedup_cap"] = round(world * world / (2 * world - 1), 3)
+    if rank == 0:
+        res["one_gpu_ms"] = round(t1, 4)
+        res["efficiency"] = round(t1 / (world * ms), 4)
+    return res
+
+
+def run_legs(world, rank, device, stream):
+    flush = l2_flush_buffer(device)
+    legs = {"cfg4": leg_cfg4(world, rank, device, 5, 3, flush, stream)}
+    layouts = ["contiguous", "zigzag"] if world > 1 else ["contiguous"]
+    legs["cfg5"] = {lay: leg_cfg5(world, rank, device, 3, 2, flush, stream, lay) for lay in layouts}
+    del flush
+    torch.cuda.empty_cache()
+    return legs
+
+
+# ----------------------------------------------------------------------------
+# single-GPU extras: naive path, peak memory, config 1
+# ----------------------------------------------------------------------------
+def naive_timing(q, k, v, sm_scale, causal, f):
+    """forward_naive with the reference benchmark's iteration counts (:129-131)."""
+    from flashlite_b200 import flash_attn_wmma as fa
+
+    N = q.shape[2]
+    warm, runs = (5, 20) if N <= 1024 else (2, 5)
+    ms = median_ms_ref_method(lambda: fa.forward_naive(q, k, v, sm_scale, causal), warm, runs)
+    return {"ms": round(ms, 4), "tflops": round(f / (ms * 1e-3) / 1e12, 3),
+            "timing": f"median of {runs} after {warm} warm-up (benchmarks/benchmark_throughput.py:129-132)"}
+
+
+def peak_memory(device, causal):
+    """benchmarks/benchmark_throughput.py:170-197 (B2 H8, N 512..4096): peak
+    allocated MB of unfused torch attention, forward_flash2 and
+    forward_flash2(out=) with q, k, v (and out) already allocated."""
+    from flashlite_b200 import flash_attn_wmma as fa
+
+    res = {}
+    for N in (512, 1024, 2048, 4096):
+        q, k, v = (torch.randn(2, 8, N, D, dtype=torch.float16, device=device) for _ in range(3))
+        buf = torch.empty_like(q)
+        sm = 1.0 / math.sqrt(D)
+
+        def peak(fn):
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats(device)
+            r = fn()
+            torch.cuda.synchronize()
+            del r
+            return round(torch.cuda.max_memory_allocated(device) / 2**20, 2)
+
+        def unfused():
+            s = torch.matmul(q, k.transpose(-2, -1)) * sm
+            return torch.matmul(torch.softmax(s, dim=-1), v)
+
+        res[str(N)] = {"unfused_torch": peak(unfused),
+                       "forward_flash2": peak(lambda: fa.forward_flash2(q, k, v, sm, causal)),
+                       "forward_flash2_out": peak(lambda: fa.forward_flash2(q, k, v, sm, causal, out=buf))}
+        del q, k, v, buf
+    torch.cuda.empty_cache()
+    return res
+
+
+def cfg1_line(device, with_cpu):
+    """BASELINE config 1 (B1 H2 N128 non-causal, seed 0, scale 1/8): GPU
+    timings of both kernels with the reference's method, and the CPU oracle."""
+    from flashlite_b200 import flash_attn_wmma as fa
+
+    B, H, N, causal, desc = WORKLOADS["cfg1"]
+    q, k, v = (t.to(device) for t in dev_slices(range(B * H), N, 0, device))
+    q, k, v = (t.view(B, H, N, D) for t in (q, k, v))
+    out = torch.empty_like(q)
+    f = flops(B, H, N, D, causal)
+    ms = median_ms_ref_method(lambda: fa.forward_flash2(q, k, v, 0.125, causal, out=out))
+    res = {"workload": desc, "flash2": {"ms": round(ms, 5), "tflops": round(f / (ms * 1e-3) / 1e12, 4)},
+           "naive": naive_timing(q, k, v, 0.125, causal, f)}
+    if with_cpu:
+        res["cpu_baseline"] = cpu_baseline("cfg1")
+    return res
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
 def run_ours(args):
     world, rank, local = dist_env()
     device = torch.device("cuda", local)
@@ -222,37 +580,49 @@ def run_ours(args):
 
     slices, total_slices, N, causal, scaling = rank_slices(args.workload, world, rank)
     S = len(slices)
-    D = 64
     sm_scale = 0.125
-    qh, kh, vh = make_inputs(slices, N, seed=0)
-    set_bytes = 4 * qh.numel() * 2
+    base = dev_slices(slices, N, seed=0, device=device)
+    shape = (1, S, N, D)
+    set_bytes = 4 * base[0].numel() * 2
     n_sets = max(2, math.ceil(3 * L2_BYTES / set_bytes))
     n_sets = min(n_sets, max(2, int(0.25 * torch.cuda.get_device_properties(device).total_memory // set_bytes)))
     sets = []
-    for i in range(n_sets):
-        if i == 0:
-            q, k, v = (t.to(device) for t in (qh, kh, vh))
-        else:  # distinct buffers, same values: keeps every step's bytes cold in L2
-            q, k, v = (t.clone() for t in sets[0][:3])
+    for i in range(n_sets):  # distinct buffers, same values: keeps every step's bytes cold in L2
+        q, k, v = (t.view(shape) if i == 0 else t.view(shape).clone() for t in base)
         sets.append((q, k, v, torch.empty_like(q)))
+    del base
     stream = torch.cuda.current_stream(device)
 
     def step(i):
         q, k, v, o = sets[i % n_sets]
         fa.forward_flash2(q, k, v, sm_scale, causal, out=o)
 
+    clk = ClockSampler(device.index if device.index is not None else 0)  # NVML set-up before timing
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(device)
     barrier(world, device)
     torch.cuda.synchronize(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index if device.index is not None else 0) as clk:
+    with clk:
+        # A ~1 ms spin on the stream before the start event: by the time the
+        # GPU reaches ev0 the host has queued all K steps, so the timed region
+        # holds device time only (no host launch latency at its start).
+        torch.cuda._sleep(2_000_000)
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
         ev1.record(stream)
         torch.cuda.synchronize(device)
+        clk.mark()
+        # untimed sustained pass of the same step (~0.3 s) for the clock reading
+        t_end = time.perf_counter() + 0.3
+        i = 0
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                step(i)
+                i += 1
+            torch.cuda.synchronize(device)
     barrier(world, device)
     torch.cuda.synchronize(device)
     ms_local = ev0.elapsed_time(ev1)
@@ -263,14 +633,30 @@ def run_ours(args):
     ms_step = ms / args.steps
     value = total_flops / (ms_step * 1e-3) / 1e12
 
+    # ---- per-call CUDA-event times: median beside the mean above ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    torch.cuda._sleep(2_000_000)
+    for i, (a, b) in enumerate(evs):
+        a.record(stream)
+        step(i)
+        b.record(stream)
+    torch.cuda.synchronize(device)
+    med_ms = max_over_ranks(median([a.elapsed_time(b) for a, b in evs]), world, device)
+
+    # ---- the reference benchmark's method: one input set, L2 warm ----
+    q0, k0, v0, o0 = sets[0]
+    same_ms = max_over_ranks(median_ms_ref_method(
+        lambda: fa.forward_flash2(q0, k0, v0, sm_scale, causal, out=o0)), world, device)
+
     # ---- end to end through the public API: pinned host in, host out ----
     # Every step copies its Q, K, V from pinned host memory and its O back.
     # Serial: copy in, compute, copy out, one after the other. Pipelined (the
     # reported e2e): two device buffer sets; step i+1's copies in run on a
     # copy stream while step i computes, step i's copy out on a third stream.
-    qp, kp, vp = (t.pin_memory() for t in (qh, kh, vh))
-    ops = [torch.empty_like(qh).pin_memory() for _ in range(2)]
-    dbuf = [tuple(torch.empty_like(sets[0][0]) for _ in range(4)) for _ in range(2)]
+    qp, kp, vp = (t.cpu().pin_memory() for t in (q0, k0, v0))
+    ops = [torch.empty_like(qp).pin_memory() for _ in range(2)]
+    dbuf = [tuple(torch.empty_like(q0) for _ in range(4)) for _ in range(2)]
 
     def e2e_serial(nsteps):
         dq, dk, dv, do = dbuf[0]
@@ -331,9 +717,22 @@ def run_ours(args):
     e2e_value = total_flops / (e_ms * 1e-3) / 1e12
     e2e_serial_value = total_flops / (es_ms * 1e-3) / 1e12
     ok = all(torch.isfinite(o.float()).all().item() for o in ops)
+    del dbuf, sets
+
+    extras = {}
+    if rank == 0 and args.workload != "cfg4":
+        extras["naive"] = naive_timing(q0, k0, v0, sm_scale, causal, per_rank_flops)
+        extras["peak_mem_mb"] = peak_memory(device, causal)
+        extras["cfg1"] = cfg1_line(device, with_cpu=(world == 1 and not args.no_cpu_baseline))
+    del q0, k0, v0, o0
+    torch.cuda.empty_cache()
+    legs = None
+    if not args.no_legs and args.workload in ("cfg3", "cfg3c"):
+        legs = run_legs(world, rank, device, stream)
 
     peak_burst, peak_sust, hbm, peak_kind = measured_peaks()
     achieved = per_rank_flops / (ms_step * 1e-3) / 1e12  # per launch per GPU
+    alg_bytes = 4 * S * N * D * 2
     traffic = profiled_traffic("flash2_fwd", args.workload)
 
     cpu = None
@@ -354,7 +753,7 @@ def run_ours(args):
             "scaling": scaling,
             "vs_baseline": None,
             "dtype": "fp16 (fp32 accumulate)",
-            "data": "synthetic: seeded i.i.d. N(0,1) fp16 Q/K/V generated on host",
+            "data": "synthetic: seeded i.i.d. N(0,1) fp16 Q/K/V generated on the device per (b,h) slice",
             "config": {
                 "workload": desc,
                 "B_per_rank": 1, "H_per_rank": S, "slices_total": total_slices,
@@ -362,16 +761,25 @@ def run_ours(args):
                 "parallelism": f"head-sharded x{world}, no collective" if world > 1 else "single GPU",
                 "l2": f"{n_sets} rotating input sets, {n_sets * set_bytes / 2**20:.0f} MiB > 126 MB L2",
             },
+            "median": {"ms_per_call": round(med_ms, 5),
+                       "value": round(total_flops / (med_ms * 1e-3) / 1e12, 2),
+                       "timing": "median of per-call CUDA-event times over K calls (same rotating sets)"},
+            "same_method": {"ms": round(same_ms, 5),
+                            "value_per_gpu": round(per_rank_flops / (same_ms * 1e-3) / 1e12, 2),
+                            "timing": "median of 100 after 25 warm-up, one input set, L2 warm "
+                                      "(benchmarks/benchmark_throughput.py:34-54)"},
             "pct_of_peak": round(100 * achieved / peak_burst, 2),
+            "hbm_gbs": round(alg_bytes / (ms_step * 1e-3) / 1e9, 1),
             "roofline": {
                 "bound": "tensor", "achieved": round(achieved, 2), "peak": peak_burst,
                 "unit": "TFLOP/s", "frac": round(achieved / peak_burst, 4),
                 "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
                 "traffic": traffic,
-                "alg_bytes": 4 * S * N * D * 2,
+                "alg_bytes": alg_bytes,
+                "hbm_frac": round(alg_bytes / (ms_step * 1e-3) / 1e9 / hbm, 4),
             },
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": 3 * qh.numel() * 2, "d2h_bytes_per_step": qh.numel() * 2,
+                    "h2d_bytes_per_step": 3 * qp.numel() * 2, "d2h_bytes_per_step": qp.numel() * 2,
                     "ms_per_step": round(e_ms, 4), "output_finite": bool(ok),
                     "mode": "pipelined: step i+1's host-to-device copies and step i-1's "
                             "device-to-host copy overlap step i's kernel (two buffer sets)",
@@ -381,6 +789,9 @@ def run_ours(args):
             "device_error": int(err),
             "cpu_baseline": cpu,
         }
+        line.update(extras)
+        if legs is not None:
+            line.update(legs)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -396,10 +807,10 @@ def run_ext(args):
     init_dist(world, "nccl")
     from flashlite_b200 import flash_attn_wmma as fa
 
-    B, H, N, D, causal, bwd, desc = EXT_WORKLOADS[args.workload]
+    B, H, N, Dx, causal, bwd, desc = EXT_WORKLOADS[args.workload]
     sm_scale = 0.0  # 1/sqrt(D)
     g = torch.Generator().manual_seed(7 + rank)
-    host = [torch.randn(B, H, N, D, generator=g).half() for _ in range(4 if bwd else 3)]
+    host = [torch.randn(B, H, N, Dx, generator=g).half() for _ in range(4 if bwd else 3)]
     tensor_bytes = host[0].numel() * 2
     in_bytes = (6 if bwd else 3) * tensor_bytes  # bwd: q, k, v, out, dout (+ lse)
     n_sets = max(2, math.ceil(3 * L2_BYTES / in_bytes))
@@ -431,11 +842,12 @@ def run_ext(args):
             step(i)
         ev1.record(stream)
         torch.cuda.synchronize(device)
+        clk.mark()
     barrier(world, device)
     ms_step = max_over_ranks(ev0.elapsed_time(ev1), world, device) / args.steps
     err = fa.device_error()
     # FLOPs: forward 4·B·H·N²·D (halved causal); backward 2.5x that (five GEMMs to two)
-    f_step = (2.5 if bwd else 1.0) * flops(B, H, N, D, causal)
+    f_step = (2.5 if bwd else 1.0) * flops(B, H, N, Dx, causal)
     value = world * f_step / (ms_step * 1e-3) / 1e12
 
     # end to end through the public API: inputs from pinned host memory, the
@@ -480,12 +892,12 @@ def run_ext(args):
     kernel = "flash2_bwd" if bwd else "flash2_fwd"
     if rank == 0:
         line = {
-            "metric": ("FA2 bwd" if bwd else "FA2 fwd") + f" TFLOP/s per B200 (fp16, D={D})",
+            "metric": ("FA2 bwd" if bwd else "FA2 fwd") + f" TFLOP/s per B200 (fp16, D={Dx})",
             "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
             "data": "synthetic: seeded i.i.d. N(0,1) fp16 inputs generated on host",
-            "config": {"workload": desc, "B": B, "H": H, "N": N, "D": D, "causal": causal,
+            "config": {"workload": desc, "B": B, "H": H, "N": N, "D": Dx, "causal": causal,
                        "sm_scale": "1/sqrt(D)",
                        "flops_per_step": f_step,
                        "parallelism": f"independent copies x{world}" if world > 1 else "single GPU",
@@ -509,7 +921,7 @@ def run_ext(args):
 
 
 # ----------------------------------------------------------------------------
-# config 5: sequence-sharded ring attention (strong scaling over ranks)
+# config 5 as the main workload: sequence-sharded ring attention
 # ----------------------------------------------------------------------------
 def run_ring(args):
     world, rank, local = dist_env()
@@ -517,107 +929,38 @@ def run_ring(args):
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
     from flashlite_b200 import flash_attn_wmma as fa
-    from flashlite_b200.parallel_attn import RingAttention, ZigzagRingAttention
 
-    B, H, N, causal, desc = WORKLOADS["cfg5"]
-    D, sm_scale = 64, 0.125
-    # causal rings use the zig-zag layout (rank r holds chunks r and 2P-1-r of
-    # 2P), which gives every rank the same work; --ring-layout contiguous keeps
-    # one contiguous block per rank
-    zigzag = world > 1 and causal and args.ring_layout == "zigzag"
-    assert N % (2 * world) == 0
-    nb = N // world
-    shape = (2, B, H, nb // 2, D) if zigzag else (B, H, nb, D)
-    g = torch.Generator(device=device).manual_seed(1000 + rank)
-    q, k, v = ((torch.randn(*shape, generator=g, device=device) * 0.5).to(torch.float16)
-               for _ in range(3))
-    out = torch.empty_like(q)
-    o_acc = torch.empty(*shape, dtype=torch.float32, device=device)
-    lse = torch.empty(*shape[:-1], dtype=torch.float32, device=device)
-    ring = (ZigzagRingAttention() if zigzag else RingAttention()) if world > 1 else None
-    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
-
-    def step():
-        if ring is None:
-            fa.forward_flash2(q, k, v, sm_scale, causal, out=out)
-        else:
-            ring.forward(q, k, v, sm_scale, causal, out=out, o_acc=o_acc, lse=lse)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(device)
-    barrier(world, device)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    stream = torch.cuda.current_stream(device)
+    flush = l2_flush_buffer(device)
     with ClockSampler(device.index) as clk:
-        for a, b in evs:
-            flush.zero_()  # untimed: evicts this rank's blocks from L2
-            a.record()
-            step()
-            b.record()
-        torch.cuda.synchronize(device)
-    barrier(world, device)
-    ms_local = sum(a.elapsed_time(b) for a, b in evs)
-    ms = max_over_ranks(ms_local, world, device)
-    ms_step = ms / args.steps
-    total_flops = flops(B, H, N, D, causal)
-    value = total_flops / (ms_step * 1e-3) / 1e12
-
-    # end to end: this rank's blocks from pinned host memory, output back
-    qp, kp, vp = (t.cpu().pin_memory() for t in (q, k, v))
-    op = torch.empty_like(qp).pin_memory()
-
-    def e2e_step():
-        q.copy_(qp, non_blocking=True)
-        k.copy_(kp, non_blocking=True)
-        v.copy_(vp, non_blocking=True)
-        step()
-        op.copy_(out, non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize(device)
-    barrier(world, device)
-    e_steps = max(2, min(args.steps, 5))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize(device)
-    e_ms = max_over_ranks(e0.elapsed_time(e1) / e_steps, world, device)
+        leg = leg_cfg5(world, rank, device, args.steps, args.warmup, flush, stream, args.ring_layout)
+        clk.mark()
     err = fa.device_error()
     peak_burst, peak_sust, _, peak_kind = measured_peaks()
-    per_gpu = value / world
     if rank == 0:
+        value = leg["tflops"]
+        per_gpu = value / world
         line = {
-            "metric": "FA2 fwd TFLOP/s per B200 (fp16, D=64)", "value": round(value, 2),
+            "metric": "FA2 fwd TFLOP/s per B200 (fp16, D=64)", "value": value,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": leg["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
-            "data": "synthetic: seeded i.i.d. N(0,1)*0.5 fp16 Q/K/V generated per rank on device",
-            "config": {"workload": desc, "B": B, "H": H, "N": N, "D": D, "causal": True,
-                       "rows_per_rank": nb,
-                       "parallelism": (f"ring x{world} (NCCL send/recv), "
-                                       f"{'zig-zag' if zigzag else 'contiguous'} layout")
-                       if world > 1 else "single GPU",
-                       "l2": "256 MiB buffer written between timed steps (untimed)"},
+            "data": "synthetic: seeded i.i.d. N(0,1)*0.5 fp16 Q/K/V generated on the device per 1024-row block",
+            "config": {"workload": WORKLOADS["cfg5"][4], "N": 131072, "D": D, "causal": True,
+                       "parallelism": (f"ring x{world} (NCCL send/recv), {args.ring_layout} layout"
+                                       if world > 1 else "single GPU"),
+                       "l2": "buffer larger than L2 written between timed steps (untimed)"},
             "pct_of_peak": round(100 * per_gpu / peak_burst, 2),
             "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peak_burst,
                          "unit": "TFLOP/s", "frac": round(per_gpu / peak_burst, 4),
                          "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
-                         "traffic": None,
-                         "note": "per GPU" + ("; causal contiguous blocks cap the ideal ring speedup at P^2/(2P-1)"
-                                           if world > 1 and causal and not zigzag else "")},
-            "e2e": {"value": round(total_flops / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": q.numel() * 2,
-                    "ms_per_step": round(e_ms, 3)},
-            "gpu_launches": args.steps * (world if world > 1 else 1),
+                         "traffic": None, "note": "per GPU"},
+            "cfg5": leg,
+            "gpu_launches": None,
             "clocks": clk.summary(),
             "device_error": int(err),
         }
         print(json.dumps(line), flush=True)
-    if ring is not None:
-        del ring
     if world > 1:
         torch.distributed.destroy_process_group()
 
@@ -626,11 +969,12 @@ def run_ring(args):
 # CPU baseline (oracle port, torch fp32 on host cores)
 # ----------------------------------------------------------------------------
 def cpu_step(workload):
-    """One bounded CPU sample of the workload: (callable, FLOPs, description).
+    """One CPU pass of the workload: (callable, FLOPs, description).
 
-    torch fp32 matmul-softmax-matmul (the oracle port). Config 5 is sampled
-    by query rows (its full score matrix would need 64 GB): the last 256 rows
-    of one head, each attending to its whole causal prefix."""
+    torch fp32 matmul-softmax-matmul (the oracle port). Configs 1-3 run in
+    full. Config 4 is sampled by slices (2 of 512) and config 5 by query rows
+    (its full score matrix would need 64 GB): the last 256 rows of one head,
+    each attending to its whole causal prefix."""
     from oracle.attention_oracle import attention_fp32, attention_rows_fp32, make_qkv
 
     B, H, N, causal, _ = WORKLOADS[workload]
@@ -642,10 +986,12 @@ def cpu_step(workload):
         f = float(sum(4 * (int(r) + 1) * 64 for r in rows))
         return (lambda: attention_rows_fp32(q3, k3, v3, rows, 0.125, True), f,
                 f"last {R} query rows of 1 of the {H} heads (N={N}, causal), row-sampled")
-    n_slices = {"cfg2": 16, "cfg2c": 16, "cfg3": 4, "cfg3c": 4, "cfg4": 1}[workload]
+    n_slices = 2 if workload == "cfg4" else B * H
     q, k, v = make_qkv(1, n_slices, N, 64, seed=0)
+    what = (f"{n_slices} of the workload's {B * H} (b,h) slices" if n_slices < B * H
+            else f"all {n_slices} (b,h) slices")
     return (lambda: attention_fp32(q, k, v, 0.125, causal), flops(1, n_slices, N, 64, causal),
-            f"{n_slices} of the workload's (b,h) slices (N={N}, causal={causal})")
+            f"{what} (N={N}, causal={causal})")
 
 
 def use_all_host_cores() -> int:
@@ -664,7 +1010,7 @@ def cpu_baseline(workload, reps=3):
         t0 = time.perf_counter()
         fn()
         ts.append(time.perf_counter() - t0)
-    t = sorted(ts)[len(ts) // 2]
+    t = median(ts)
     return {"value": round(f / t / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
             "sample": f"{desc}; torch fp32 matmul-softmax-matmul, median of {reps}: {t * 1e3:.1f} ms"}
@@ -692,7 +1038,8 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic: seeded i.i.d. N(0,1) fp16 Q/K/V generated on host",
         "config": {"workload": WORKLOADS[args.workload][4], "sample": desc, "N": N,
-                   "D": 64, "causal": causal},
+                   "D": 64, "causal": causal,
+                   "same_config": args.workload in ("cfg1", "cfg2", "cfg2c", "cfg3", "cfg3c")},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s",
                          "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -705,40 +1052,30 @@ def run_reference(args):
 def reference_gpu(workload):
     """Times the reference's WMMA kernels (built from its own sources for
     sm_100a into oracle/_ref) and PyTorch SDPA-flash, the reference's own
-    comparator (benchmarks/benchmark_throughput.py:99-104), on this GPU."""
+    comparator (benchmarks/benchmark_throughput.py:99-104), on this GPU, with
+    the reference benchmark's method. Loads nothing of this package."""
     if not torch.cuda.is_available():
         return {"unavailable": "no GPU"}
     from oracle import build_ref
 
     B, H, N, causal, _ = WORKLOADS[workload]
-    if workload == "cfg4":
-        return {"unavailable": "not timed for cfg4"}
+    if workload in ("cfg4", "cfg5"):
+        return {"unavailable": f"not timed for {workload}"}
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
     q, k, v = (torch.randn(B, H, N, 64, device=dev, dtype=torch.float16, generator=g) for _ in range(3))
     out = torch.empty_like(q)
     f = flops(B, H, N, 64, causal)
-
-    def median_ms(fn, warm=25, runs=100):  # benchmarks/benchmark_throughput.py:34-54
-        for _ in range(warm):
-            fn()
-        torch.cuda.synchronize()
-        es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(runs)]
-        for a, b in es:
-            a.record()
-            fn()
-            b.record()
-        torch.cuda.synchronize()
-        ts = sorted(a.elapsed_time(b) for a, b in es)
-        return ts[len(ts) // 2]
-
     res = {"timing": "median of 100 after 25 warm-up, L2 warm (the reference benchmark's method)"}
     mod = build_ref.load()
     if mod is None:
         res["wmma"] = {"unavailable": "oracle/_ref not built"}
     else:
-        ms = median_ms(lambda: mod.forward_flash2(q, k, v, 0.125, causal, out=out))
+        ms = median_ms_ref_method(lambda: mod.forward_flash2(q, k, v, 0.125, causal, out=out))
         res["wmma"] = {"ms": round(ms, 4), "tflops": round(f / ms / 1e9, 2)}
+        warm, runs = (5, 20) if N <= 1024 else (2, 5)
+        ms = median_ms_ref_method(lambda: mod.forward_naive(q, k, v, 0.125, causal), warm, runs)
+        res["naive"] = {"ms": round(ms, 4), "tflops": round(f / ms / 1e9, 3)}
     try:
         from torch.nn.attention import SDPBackend, sdpa_kernel
         import torch.nn.functional as F
@@ -747,27 +1084,25 @@ def reference_gpu(workload):
             with sdpa_kernel([SDPBackend.FLASH_ATTENTION]):
                 return F.scaled_dot_product_attention(q, k, v, is_causal=causal, scale=0.125)
 
-        ms = median_ms(sdpa)
+        ms = median_ms_ref_method(sdpa)
         res["sdpa_flash"] = {"ms": round(ms, 4), "tflops": round(f / ms / 1e9, 2)}
     except Exception as exc:  # backend may be unavailable
         res["sdpa_flash"] = {"unavailable": str(exc)[:120]}
-    from flashlite_b200 import flash_attn_wmma as fa
-
-    ms = median_ms(lambda: fa.forward_flash2(q, k, v, 0.125, causal, out=out))
-    res["flashlite_b200_same_method"] = {"ms": round(ms, 4), "tflops": round(f / ms / 1e9, 2)}
     return res
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg3", choices=sorted(WORKLOADS) + sorted(EXT_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ring-layout", default="zigzag", choices=["zigzag", "contiguous"],
-                    help="sequence layout of the config-5 ring on 2+ GPUs")
+    ap.add_argument("--no-legs", action="store_true",
+                    help="skip the config-4 / config-5 sub-measurements of the config-3 workloads")
+    ap.add_argument("--ring-layout", default="contiguous", choices=["contiguous", "zigzag"],
+                    help="sequence layout of --workload cfg5 on 2+ GPUs (config 5 fixes contiguous blocks)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -23,7 +23,8 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 
-CUDA_SOURCES = ["fl_api.cu", "fl_flash2.cu", "fl_flash2_bwd.cu", "fl_naive.cu", "fl_noalloc.cu"]
+CUDA_SOURCES = ["fl_api.cu", "fl_flash2.cu", "fl_flash2_bwd.cu", "fl_naive.cu", "fl_noalloc.cu",
+                "fl_selftest.cu"]
 HEADERS = ["fl_ptx.cuh", "fl_internal.h"]
 LIB = PKG / "libflashlite_b200.so"
 EXT = PKG / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))

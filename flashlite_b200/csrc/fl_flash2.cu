@@ -120,6 +120,10 @@ __host__ __device__ constexpr int poly_cols(int cols) {
 }
 static_assert(poly_cols(64) >= 8 && poly_cols(64) <= 56, "both exp methods must get columns");
 
+#ifndef FL_MMA_WARP
+#define FL_MMA_WARP 1
+#endif
+
 // Maximum of N values in four independent chains of 3-input max.
 template <int N>
 __device__ __forceinline__ float max_chains4(const float* v) {
@@ -198,6 +202,14 @@ __device__ long long fl_trace_buf[kTraceEvents * kTraceIters];
     if (blockIdx.x == 0 && (it) < kTraceIters)                                     \
       fl_trace_buf[(ev) * kTraceIters + (it)] = clock64();                         \
   } while (0)
+}  // namespace
+// Host read-out of the trace (trace builds only).
+extern "C" int fl_trace_read(long long* host, int n) {
+  const int total = kTraceEvents * kTraceIters;
+  return cudaMemcpyFromSymbol(host, fl_trace_buf, sizeof(long long) * (n < total ? n : total)) == cudaSuccess
+             ? 0 : -1;
+}
+namespace {
 #else
 #define FL_TRACE_EV(ev, it) \
   do {                      \
@@ -410,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
                : produce_ring<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv, bh % p.nh,
                                             bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
-  } else if (warp == 1) {
+  } else if (warp == FL_MMA_WARP) {
     // ======================= MMA issuer =======================
     constexpr uint32_t idesc_s = make_idesc_f16_f32(kBM, kBN, false);  // K-major A and B
     constexpr uint32_t idesc_pv = make_idesc_f16_f32(kBM, kD, true);   // B (= V) MN-major
@@ -477,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       // P_1(j-1) V, S_1(j+1), P_0(j) V. Each MMA waits only for its own
       // inputs, so neither tile's softmax waits behind the other's.
       for (int j = 0; j <= nkv; ++j) {
+        if (lane == 0) FL_TRACE_EV(19, j);
         const bool s_next = j + 1 < nkv;
         const int rk0 = ring(0, j + 1);
         const int sk = rk0 % kStagesK;
@@ -513,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
           if (!warp_wait_issuer(bar_sfree(1), j & 1, abort_flag, p.err)) break;
           tc_fence_after();
           issue_s(1, sk1);
+          if (lane == 0) FL_TRACE_EV(18, j);
         }
         if (kSplit ? (j + 1 < nkv1) : s_next) commit_to(bar_kempty(sk1));
         if (j < nkv) {
@@ -567,6 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
     if (i == 1 && my_nkv > 0) ok = warp_wait(bar_stagger, 0, abort_flag, p.err);
 
     for (int j = 0; ok && j < my_nkv; ++j) {
+      if (t == 0 && i == 0) FL_TRACE_EV(19, j);
       if (!warp_wait(bar_s(i), j & 1, abort_flag, p.err)) { ok = false; break; }
       if (t == 0) FL_TRACE_EV(0 + 4 * i, j);
       tc_fence_after();
@@ -640,6 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         // rewritten and before O is rescaled.
         if (!warp_wait(bar_pv(i), (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
+        if (t == 0) FL_TRACE_EV(16 + i, j);
         if (__any_sync(0xffffffffu, need)) {
           uint32_t o[32];
 #pragma unroll
@@ -900,14 +916,9 @@ template <int HD, bool kCausal, bool kMerge, bool kSplit = false>
 cudaError_t launch_variant(const Flash2Params& prm, int grid, cudaStream_t stream) {
   constexpr int kSmemAlloc = Cfg<HD>::kSmemAlloc;
   auto kern = flash2_fwd_kernel<HD, kCausal, kMerge, kSplit>;
-  static int configured_mask = 0;  // bit per device (up to 32 devices)
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured_mask & (1 << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
-    if (e != cudaSuccess) return e;
-    configured_mask |= (1 << (dev & 31));
-  }
+  static std::atomic<bool> configured[kMaxFlagDevices];
+  const cudaError_t e = ensure_smem_limit(kern, kSmemAlloc, configured);
+  if (e != cudaSuccess) return e;
   // Launched with programmatic stream serialization (see griddepcontrol in
   // the kernel): back-to-back calls overlap one's set-up with the previous
   // one's last wave (config 2 262 -> 312 TF/s, config 3 643 -> 658).

@@ -510,14 +510,9 @@ bool encode_dq_map(CUtensorMap* tm, float* base, int64_t n, int64_t H, int64_t B
 template <bool kCausal>
 cudaError_t launch_bwd_variant(const BwdParams& prm, int grid, cudaStream_t stream) {
   auto kern = flash2_bwd_kernel<kCausal>;
-  static int configured_mask = 0;  // bit per device (up to 32 devices)
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured_mask & (1 << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
-    if (e != cudaSuccess) return e;
-    configured_mask |= (1 << (dev & 31));
-  }
+  static std::atomic<bool> configured[kMaxFlagDevices];
+  const cudaError_t e = ensure_smem_limit(kern, kSmemAlloc, configured);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <string>
 
@@ -14,6 +15,25 @@ const char* last_error();
 
 // Device-side error word of the current device (address in device memory).
 unsigned int* device_error_word();
+
+// Raises `kern`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per device and kernel. Thread-safe: `done` (one per kernel
+// instantiation, static storage) records the devices already configured; two
+// threads may both configure a device the first time, which is harmless
+// (cudaFuncSetAttribute is idempotent). Devices past kMaxFlagDevices are
+// configured on every call.
+constexpr int kMaxFlagDevices = 64;
+template <typename Kernel>
+cudaError_t ensure_smem_limit(Kernel kern, int bytes, std::atomic<bool> (&done)[kMaxFlagDevices]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool tracked = dev >= 0 && dev < kMaxFlagDevices;
+  if (tracked && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && tracked) done[dev].store(true, std::memory_order_release);
+  return e;
+}
 
 // Number of SMs of the current device (cached per device).
 int sm_count();

@@ -84,14 +84,16 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity
 
 // Bounded wait for phase `parity` of `bar`. Returns false (after recording
 // kDevErrWaitTimeout in *err and raising the CTA abort flag) if the phase does
-// not complete within FL_WAIT_LIMIT_NS, or if another role of this CTA has
-// already aborted. Never waits forever. Waiting threads sleep in try_wait
-// (suspend hint `hint_ns`) and look at the clock and the abort flag only
-// every 16 probes, so a waiting warp takes almost no issue slots from the
-// warps that are working.
+// not complete within `limit_ns` (FL_WAIT_LIMIT_NS in every kernel of the
+// library; the bounded-wait self-test passes a short one), or if another role
+// of this CTA has already aborted. Never waits forever. Waiting threads sleep
+// in try_wait (suspend hint `hint_ns`) and look at the clock and the abort
+// flag only every 16 probes, so a waiting warp takes almost no issue slots
+// from the warps that are working.
 __device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity,
                                                  volatile int* abort_flag, unsigned int* err,
-                                                 uint32_t hint_ns) {
+                                                 uint32_t hint_ns,
+                                                 uint64_t limit_ns = FL_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -99,7 +101,7 @@ __device__ __forceinline__ bool mbar_wait_hinted(uint32_t bar, uint32_t parity,
     for (int k = 0; k < 16; ++k)
       if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > FL_WAIT_LIMIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (err) atomicOr(err, kDevErrWaitTimeout);
       return false;

@@ -106,9 +106,6 @@ torch::Tensor forward_naive(torch::Tensor q, torch::Tensor k, torch::Tensor v, d
   return out;
 }
 
-// One ring-attention block step (no reference counterpart): merges
-// attention of q [B,H,Nq,64] against k/v [B,H,Nk,64] into (o_acc fp32
-// [B,H,Nq,64], lse fp32 [B,H,Nq]).
 // Extension without a reference counterpart: N_k != N_q, position offsets,
 // optional LSE output (fl_flash2_fwd_ex). Returns (out, lse); lse is an
 // empty tensor unless return_lse.
@@ -156,6 +153,9 @@ std::vector<torch::Tensor> forward_flash2_ex(torch::Tensor q, torch::Tensor k, t
   return {out_tensor, lse};
 }
 
+// One ring-attention block step (no reference counterpart): merges
+// attention of q [B,H,Nq,64] against k/v [B,H,Nk,64] into (o_acc fp32
+// [B,H,Nq,64], lse fp32 [B,H,Nq]).
 void forward_block(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o_acc,
                    torch::Tensor lse, int64_t q_offset, int64_t kv_offset, double sm_scale,
                    bool is_causal, bool first) {

@@ -52,6 +52,21 @@ def head_sharded_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_s
 BlockFn = Callable[..., None]
 
 
+def _step_events(events: Optional[list]):
+    """Three timing events for one ring step (the first recorded now), or None."""
+    if events is None:
+        return None
+    ev = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
+    ev[0].record()
+    events.append(ev)
+    return ev
+
+
+def _record(ev, i: int) -> None:
+    if ev is not None:
+        ev[i].record()
+
+
 def _default_block_fn():
     from . import flash_attn_wmma as fa
 
@@ -101,7 +116,12 @@ class RingAttention:
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float = 0.0,
                 is_causal: bool = True, out: Optional[torch.Tensor] = None,
                 o_acc: Optional[torch.Tensor] = None,
-                lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+                lse: Optional[torch.Tensor] = None, events: Optional[list] = None) -> torch.Tensor:
+        """``events``: if a list, one (start, computed, received) triple of
+        timing CUDA events is appended per ring step, recorded on the current
+        stream before the step's block compute, after it, and after the wait
+        for the next K/V block (so received - computed is exchange time the
+        compute did not hide)."""
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         if q.shape != k.shape or k.shape != v.shape:
@@ -127,11 +147,14 @@ class RingAttention:
                        dist.P2POp(dist.irecv, nk, g_prv, self.group),
                        dist.P2POp(dist.irecv, nv, g_prv, self.group)]
                 reqs = dist.batch_isend_irecv(ops)
+            ev = _step_events(events)
             if compute:
                 self.block_fn(q, cur_k, cur_v, o_acc, lse, rank * Nb, src * Nb, sm_scale,
                               is_causal, s == 0)
+            _record(ev, 1)
             for r in reqs:
                 r.wait()
+            _record(ev, 2)
             if s < world - 1:
                 cur_k, cur_v = nk, nv
         self.finalize_fn(o_acc, out)
@@ -172,7 +195,7 @@ class ZigzagRingAttention(RingAttention):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float = 0.0,
                 is_causal: bool = True, out: Optional[torch.Tensor] = None,
                 o_acc: Optional[torch.Tensor] = None,
-                lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+                lse: Optional[torch.Tensor] = None, events: Optional[list] = None) -> torch.Tensor:
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         if q.shape != k.shape or k.shape != v.shape or q.dim() != 5 or q.shape[0] != 2:
@@ -201,12 +224,15 @@ class ZigzagRingAttention(RingAttention):
                        dist.P2POp(dist.irecv, nxt_buf, g_prv, self.group)]
                 reqs = dist.batch_isend_irecv(ops)
             kc = zigzag_chunks(src, world)
+            ev = _step_events(events)
             for a, b in zigzag_pairs(rank, src, world, is_causal):
                 self.block_fn(q[a], cur[0, b], cur[1, b], o_acc[a], lse[a], own[a] * c, kc[b] * c,
                               sm_scale, is_causal, not started[a])
                 started[a] = True
+            _record(ev, 1)
             for r in reqs:
                 r.wait()
+            _record(ev, 2)
             if s < world - 1:
                 cur = nxt_buf
         for a in range(2):

@@ -152,6 +152,23 @@ const char* fl_last_error(void);
  */
 int fl_device_error(void* stream, uint32_t* flags);
 
+/*
+ * Self-test of the bounded-wait failure path. No reference counterpart: the
+ * reference's only error path is CUDA_CHECK after a launch
+ * (csrc/includes/flash_attn.h:15-22). Every wait inside this library's
+ * kernels is bounded; this entry point makes one run out on purpose, in the
+ * form a kernel can survive: one CTA of two warps on `stream`, each waiting
+ * on its own mbarrier that nothing ever arrives on. Warp 0 waits at most
+ * `limit_ns` (1 .. 1e9 ns), then records the timeout in the device error word
+ * and raises its CTA's abort flag; warp 1 waits with the library's normal
+ * limit (2 s) but sees the abort flag and returns early, as every role of the
+ * attention kernels does. `out` (device memory, 4 x uint64) receives warp 0's
+ * wait result (1 = completed, 0 = gave up), its wait time in ns, then the same
+ * two values of warp 1. Afterwards fl_device_error() returns
+ * FL_ERR_DEVICE_TIMEOUT and the device stays usable.
+ */
+int fl_selftest_bounded_wait(uint64_t limit_ns, uint64_t* out, void* stream);
+
 /* Library version as "major.minor.patch". */
 const char* fl_version(void);
 

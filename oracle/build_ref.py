@@ -13,6 +13,10 @@ inputs, and by ``bench.py --impl reference`` to time them beside the CPU
 baseline. Needs the reference tree, so it only runs in the build container;
 the built .so travels to GPU boxes with the repository snapshot.
 
+The reference root comes from the command line or the FLASHLITE_REFERENCE
+environment variable; ``build_if_available`` also looks for a ``reference``
+directory beside this repository's own directory.
+
 Run: python -m oracle.build_ref  [reference_root]
 """
 from __future__ import annotations
@@ -26,7 +30,6 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 MODULE = "flash_attn_wmma"
-DEFAULT_REF = Path(os.environ.get("FLASHLITE_REFERENCE", "/root/reference"))
 EXT = OUT_DIR / (MODULE + sysconfig.get_config_var("EXT_SUFFIX"))
 
 # setup.py:39-48 of the reference, with -arch retargeted to sm_100a
@@ -43,7 +46,17 @@ def _run(cmd):
         raise RuntimeError(f"reference build failed:\n{' '.join(cmd)}\n{r.stdout}{r.stderr}")
 
 
-def build(ref_root: Path = DEFAULT_REF) -> Path:
+def reference_root() -> Path | None:
+    """The reference tree: $FLASHLITE_REFERENCE, else ``../reference`` next to
+    this repository; None when neither holds the reference's sources."""
+    env = os.environ.get("FLASHLITE_REFERENCE")
+    for cand in ([Path(env)] if env else []) + [HERE.parent.parent / "reference"]:
+        if (cand / "csrc" / "kernel_flash2.cu").exists():
+            return cand
+    return None
+
+
+def build(ref_root: Path) -> Path:
     import torch
     from torch.utils import cpp_extension as ce
 
@@ -86,10 +99,11 @@ def build_if_available() -> Path | None:
     """Build when the reference tree is present and the module is missing."""
     if EXT.exists():
         return EXT
-    if not (DEFAULT_REF / "csrc" / "kernel_flash2.cu").exists():
+    root = reference_root()
+    if root is None:
         return None
     try:
-        return build(DEFAULT_REF)
+        return build(root)
     except Exception as exc:  # the checker is optional; the product build is not
         print(f"oracle/_ref not built: {exc}", file=sys.stderr)
         return None
@@ -110,5 +124,7 @@ def load():
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        sys.exit("reference tree not found: pass its path or set FLASHLITE_REFERENCE")
     print("built", build(root))

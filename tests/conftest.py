@@ -61,4 +61,6 @@ def fl_lib():
     lib.fl_version.restype = ctypes.c_char_p
     lib.fl_device_error.argtypes = [p, ctypes.POINTER(ctypes.c_uint32)]
     lib.fl_device_error.restype = i32
+    lib.fl_selftest_bounded_wait.argtypes = [ctypes.c_uint64, p, p]
+    lib.fl_selftest_bounded_wait.restype = i32
     return lib

@@ -16,7 +16,8 @@ FL_OK, FL_ERR_INVALID_ARGUMENT, FL_ERR_UNSUPPORTED = 0, 1, 2
 def test_header_declares_expected_api(header_fns):
     for name in ("fl_flash2_fwd", "fl_naive_fwd", "fl_flash2_fwd_block", "fl_ring_finalize",
                  "fl_status_str", "fl_last_error", "fl_device_error", "fl_version",
-                 "fl_flash2_fwd_ex", "fl_flash2_bwd", "fl_flash2_bwd_workspace_size"):
+                 "fl_flash2_fwd_ex", "fl_flash2_bwd", "fl_flash2_bwd_workspace_size",
+                 "fl_selftest_bounded_wait"):
         assert name in header_fns
 
 
@@ -117,3 +118,14 @@ def test_backward_binding_rejects_cpu_tensors():
     with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
         fa.backward_flash2(q, k, v, q, q, lse)
     assert "is_causal" in fa.backward_flash2.__doc__ and "sm_scale" in fa.backward_flash2.__doc__
+
+
+def test_selftest_bounded_wait_rejects_bad_arguments(fl_lib):
+    """Checked before any device work: a null result buffer, a zero limit and
+    a limit above one second are refused."""
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    assert fl_lib.fl_selftest_bounded_wait(1000, None, None) == FL_ERR_INVALID_ARGUMENT
+    assert fl_lib.fl_selftest_bounded_wait(0, p, None) == FL_ERR_INVALID_ARGUMENT
+    assert fl_lib.fl_selftest_bounded_wait(2_000_000_000, p, None) == FL_ERR_INVALID_ARGUMENT
+    assert b"limit_ns" in fl_lib.fl_last_error()

@@ -99,7 +99,10 @@ def test_multi_block_sequence_matches_full_attention(cuda, lib):
 def test_call_allocates_no_device_memory(cuda, lib):
     q, k, v = (t.to(cuda) for t in orc.make_qkv(1, 2, 256, 64, seed=5))
     o = torch.empty_like(q)
-    _noalloc(lib, q, k, v, o, 0, 0, True, True, True)  # first call on the device: set-up
+    # The first call on the device does the set-up (symbol lookup) and, being
+    # the same launch as the loop below, also loads every kernel the loop
+    # uses, so nothing lazily loaded can show up as device memory later.
+    _noalloc(lib, q, k, v, o, 0, 0, True, True, True)
     torch.cuda.synchronize()
     gc.collect()  # tensors of earlier tests still waiting for collection
     free0, _ = torch.cuda.mem_get_info()
@@ -107,9 +110,12 @@ def test_call_allocates_no_device_memory(cuda, lib):
     for _ in range(3):
         _noalloc(lib, q, k, v, o, 0, 0, True, True, True)
     torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info()[0] == free0
     # torch may free (never allocate) blocks of earlier tests meanwhile
     assert torch.cuda.memory_allocated() <= torch_alloc0
+    # Device-wide free memory also counts other contexts on the GPU, so it is
+    # compared with slack: an allocation by these calls would be at least the
+    # 2 MiB allocation granule.
+    assert torch.cuda.mem_get_info()[0] >= free0 - (1 << 20)
 
 
 def test_rejects_sizes_beyond_the_array(cuda, lib):
