@@ -120,10 +120,6 @@ __host__ __device__ constexpr int poly_cols(int cols) {
 }
 static_assert(poly_cols(64) >= 8 && poly_cols(64) <= 56, "both exp methods must get columns");
 
-#ifndef FL_MMA_WARP
-#define FL_MMA_WARP 1
-#endif
-
 // Maximum of N values in four independent chains of 3-input max.
 template <int N>
 __device__ __forceinline__ float max_chains4(const float* v) {
@@ -422,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
                : produce_ring<HD, kStagesV>(&p.tm_v, s_v0, bar_vfull0, bar_vempty0, nkv, bh % p.nh,
                                             bh / p.nh, lane, abort_flag, p.err);
     if (*abort_flag && lane == 0) drain_ring<kStagesV>(bar_vfull0, issued);
-  } else if (warp == FL_MMA_WARP) {
+  } else if (warp == 1) {
     // ======================= MMA issuer =======================
     constexpr uint32_t idesc_s = make_idesc_f16_f32(kBM, kBN, false);  // K-major A and B
     constexpr uint32_t idesc_pv = make_idesc_f16_f32(kBM, kD, true);   // B (= V) MN-major
