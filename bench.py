@@ -493,11 +493,23 @@ def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
     return res
 
 
+def _leg(fn, *a):
+    """Runs one leg; an exception is recorded in the leg's own entry so that
+    the line still carries the headline. (A failure on every rank leaves the
+    ranks in step; one on a single rank ends its peers' next collective
+    through the process group's timeout.)"""
+    try:
+        return fn(*a)
+    except Exception as exc:  # reported, not hidden: the entry says what failed
+        torch.cuda.synchronize()
+        return {"error": f"{type(exc).__name__}: {str(exc)[:300]}"}
+
+
 def run_legs(world, rank, device, stream):
     flush = l2_flush_buffer(device)
-    legs = {"cfg4": leg_cfg4(world, rank, device, 5, 3, flush, stream)}
+    legs = {"cfg4": _leg(leg_cfg4, world, rank, device, 5, 3, flush, stream)}
     layouts = ["contiguous", "zigzag"] if world > 1 else ["contiguous"]
-    legs["cfg5"] = {lay: leg_cfg5(world, rank, device, 3, 2, flush, stream, lay) for lay in layouts}
+    legs["cfg5"] = {lay: _leg(leg_cfg5, world, rank, device, 3, 2, flush, stream, lay) for lay in layouts}
     del flush
     torch.cuda.empty_cache()
     return legs
