@@ -416,8 +416,18 @@ def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
     o_acc = torch.empty(q.shape, dtype=torch.float32, device=device)
     lse = torch.empty(q.shape[:-1], dtype=torch.float32, device=device)
     ring = None
+    launches = [0]  # this rank's kernel launches in its timed steps
     if world > 1:
-        ring = ZigzagRingAttention() if layout == "zigzag" else RingAttention()
+        def block(*a):
+            launches[0] += 1
+            fa.forward_block(*a)
+
+        def finalize(*a):
+            launches[0] += 1
+            fa.ring_finalize(*a)
+
+        cls = ZigzagRingAttention if layout == "zigzag" else RingAttention
+        ring = cls(block_fn=block, finalize_fn=finalize)
 
     def step(events=None):
         if ring is None:
@@ -426,6 +436,7 @@ def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
             ring.forward(q, k, v, sm_scale, causal, out=out, o_acc=o_acc, lse=lse, events=events)
 
     ts = time_steps_flushed(step, steps, warmup, flush, stream)
+    per_step = launches[0] / (steps + warmup) if ring is not None else 1.0
     ms = max_over_ranks(median(ts), world, device)
     breakdown = None
     if ring is not None:
@@ -480,6 +491,7 @@ def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
     f = flops(B, H, N, D, causal)
     res = {"workload": desc, "scaling": "strong",
            "layout": (layout if world > 1 else "single GPU"),
+           "gpu_launches_per_step": per_step,
            "ms_per_step": round(ms, 4), "tflops": round(f / (ms * 1e-3) / 1e12, 2),
            "timing": f"median of {steps} steps after {warmup} warm-up, L2 flushed between steps, max over ranks",
            "parity": parity}
@@ -968,7 +980,7 @@ def run_ring(args):
                          "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
                          "traffic": None, "note": "per GPU"},
             "cfg5": leg,
-            "gpu_launches": None,
+            "gpu_launches": int(round(args.steps * leg["gpu_launches_per_step"])),
             "clocks": clk.summary(),
             "device_error": int(err),
         }
