@@ -513,7 +513,8 @@ def _leg(fn, *a):
     try:
         return fn(*a)
     except Exception as exc:  # reported, not hidden: the entry says what failed
-        torch.cuda.synchronize()
+        if torch.cuda.is_available() and torch.cuda.is_initialized():
+            torch.cuda.synchronize()
         return {"error": f"{type(exc).__name__}: {str(exc)[:300]}"}
 
 

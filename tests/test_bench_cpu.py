@@ -88,3 +88,11 @@ def test_reference_arm_loads_no_package_code():
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["config"]["same_config"] is True
     assert line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_failed_leg_is_reported_in_its_own_entry():
+    def broken(*_):
+        raise RuntimeError("leg failed")
+
+    assert bench._leg(broken, 1, 2) == {"error": "RuntimeError: leg failed"}
+    assert bench._leg(lambda a, b: {"ok": a + b}, 1, 2) == {"ok": 3}
