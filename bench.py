@@ -640,10 +640,11 @@ def run_ours(args):
     torch.cuda.synchronize(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with clk:
-        # A ~1 ms spin on the stream before the start event: by the time the
-        # GPU reaches ev0 the host has queued all K steps, so the timed region
-        # holds device time only (no host launch latency at its start).
-        torch.cuda._sleep(2_000_000)
+        # A ~4 ms spin on the stream before the start event: by the time the
+        # GPU reaches ev0 the host has queued all K steps (~25 us each through
+        # the binding, with the clock sampler's thread sharing the GIL), so
+        # the timed region holds device time only.
+        torch.cuda._sleep(8_000_000)
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
@@ -671,7 +672,7 @@ def run_ours(args):
     # ---- per-call CUDA-event times: median beside the mean above ----
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
-    torch.cuda._sleep(2_000_000)
+    torch.cuda._sleep(8_000_000)
     for i, (a, b) in enumerate(evs):
         a.record(stream)
         step(i)
