@@ -404,6 +404,27 @@ def ring_inputs(world, rank, layout, N, H, seed, scale, device):
     return q, k, v, [rank * nb], nb
 
 
+def ring_breakdown(per, ms):
+    """Names the step that limits a ring from every rank's [compute ms,
+    exchange-wait ms] of one step and the step time: the rank that computes
+    most sets the step, so its wait is exchange the ring failed to hide
+    (lightly loaded ranks also wait, on their busier neighbours)."""
+    comp = [c for c, _ in per]
+    crit = max(range(len(per)), key=lambda r: comp[r])
+    c_max, c_min = max(comp), min(comp)
+    out = {"compute_ms_max": round(c_max, 4), "compute_ms_min": round(c_min, 4),
+           "exposed_exchange_ms_max": round(max(w for _, w in per), 4),
+           "busiest_rank": crit, "busiest_rank_exchange_wait_ms": round(per[crit][1], 4)}
+    if per[crit][1] > 0.1 * ms:
+        out["limiting_step"] = "K/V exchange not hidden behind the busiest rank's block compute"
+    elif c_max > 1.15 * c_min:
+        out["limiting_step"] = ("causal load imbalance: the rank holding the last rows computes "
+                                f"{c_max / max(c_min, 1e-9):.2f}x the lightest rank's blocks")
+    else:
+        out["limiting_step"] = "block compute (the ring's per-step kernel launches on N/P-row blocks)"
+    return out
+
+
 def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
     """B1 H8 N131072 causal, sequence sharded over ranks."""
     from flashlite_b200 import flash_attn_wmma as fa
@@ -454,21 +475,7 @@ def leg_cfg5(world, rank, device, steps, warmup, flush, stream, layout):
         per[rank, 0], per[rank, 1] = comp, wait
         if world > 1:
             torch.distributed.all_reduce(per)
-        per = per.cpu()
-        crit = int(per[:, 0].argmax())
-        c_max, c_min = float(per[:, 0].max()), float(per[:, 0].min())
-        breakdown = {"compute_ms_max": round(c_max, 4), "compute_ms_min": round(c_min, 4),
-                     "exposed_exchange_ms_max": round(float(per[:, 1].max()), 4),
-                     "busiest_rank": crit,
-                     "busiest_rank_exchange_wait_ms": round(float(per[crit, 1]), 4)}
-        if per[crit, 1] > 0.1 * ms:
-            limit = "K/V exchange not hidden behind the busiest rank's block compute"
-        elif c_max > 1.15 * c_min:
-            limit = ("causal load imbalance: the rank holding the last rows computes "
-                     f"{c_max / max(c_min, 1e-9):.2f}x the lightest rank's blocks")
-        else:
-            limit = "block compute (the ring's per-step kernel launches on N/P-row blocks)"
-        breakdown["limiting_step"] = limit
+        breakdown = ring_breakdown(per.cpu().tolist(), ms)
     # parity: sampled rows of this rank (first and last rows of each part) on
     # the first and last head, against the oracle over the whole causal prefix
     errs = []

@@ -96,3 +96,32 @@ def test_failed_leg_is_reported_in_its_own_entry():
 
     assert bench._leg(broken, 1, 2) == {"error": "RuntimeError: leg failed"}
     assert bench._leg(lambda a, b: {"ok": a + b}, 1, 2) == {"ok": 3}
+
+
+def test_ring_breakdown_names_the_limit():
+    # 4 ranks of a contiguous causal ring: the light ranks wait on their
+    # neighbours, the busiest hardly at all -> imbalance, not the exchange
+    per = [[1.5, 6.3], [4.0, 4.0], [7.0, 1.2], [9.8, 0.3]]
+    out = bench.ring_breakdown(per, 11.0)
+    assert out["busiest_rank"] == 3 and out["limiting_step"].startswith("causal load imbalance")
+    # the busiest rank waits > 10 % of the step: the exchange is exposed
+    assert bench.ring_breakdown([[9.8, 2.0], [9.5, 0.1]], 11.0)["limiting_step"].startswith("K/V exchange")
+    # balanced, hidden exchange: block compute
+    assert bench.ring_breakdown([[6.4, 0.01], [6.5, 0.01]], 6.5)["limiting_step"].startswith("block compute")
+
+
+def test_leg_parity_check_flags_a_wrong_output():
+    """The legs' row check against the oracle: exact rows pass, a mistake
+    planted in the compared output (on the CPU) fails the tolerance."""
+    from oracle.attention_oracle import attention_rows_fp32
+
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 512, 64, generator=g).half() for _ in range(3))
+    rows = torch.tensor([0, 100, 511])
+    good = attention_rows_fp32(q, k, v, rows, 0.125, True).half()
+    e = bench.row_errors(good, q, k, v, rows, 0.125, True)
+    ok = bench.reduce_errors([e], 1, None)
+    assert ok["ok"] and ok["values_checked"] == 3 * 64
+    bad = good.clone()
+    bad[0, 1, 5] += 0.01
+    assert not bench.reduce_errors([bench.row_errors(bad, q, k, v, rows, 0.125, True)], 1, None)["ok"]
