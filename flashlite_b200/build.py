@@ -23,9 +23,9 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 
-CUDA_SOURCES = ["fl_api.cu", "fl_flash2.cu", "fl_flash2_bwd.cu", "fl_naive.cu", "fl_noalloc.cu",
-                "fl_selftest.cu"]
-HEADERS = ["fl_ptx.cuh", "fl_internal.h"]
+CUDA_SOURCES = ["fl_api.cu", "fl_flash2.cu", "fl_flash2_sk.cu", "fl_flash2_bwd.cu", "fl_naive.cu",
+                "fl_noalloc.cu", "fl_selftest.cu"]
+HEADERS = ["fl_ptx.cuh", "fl_internal.h", "fl_flash2_common.cuh"]
 LIB = PKG / "libflashlite_b200.so"
 EXT = PKG / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
