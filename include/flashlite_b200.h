@@ -40,6 +40,12 @@ typedef enum fl_status {
  * q, k, v, o: [B, H, N, D] fp16, D must be 64 (csrc/kernel_flash2.cu:756-757).
  * sm_scale == 0 selects 1/sqrt(D) (csrc/kernel_flash2.cu:769-771).
  * is_causal != 0 masks keys j > query i. o may not alias q, k or v.
+ * Device memory: a non-causal call whose grid would leave part of its last
+ * wave idle may run the stream-K schedule; the first such call on a stream
+ * allocates that stream's 19.7 MB workspace (cudaMalloc, kept until exit;
+ * never while the stream is being captured: the call then runs the other
+ * schedule). FL_STREAMK=0 in the environment turns the schedule off. The
+ * same holds for fl_flash2_fwd_ex.
  */
 int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
                   int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);
