@@ -76,6 +76,8 @@ EXT_WORKLOADS = {
     "bwd3c": (2, 8, 4096, 64, True, True, "FA2 backward on the config-3 shape: B2 H8 N4096 D64 causal"),
     "d128_3": (2, 8, 4096, 128, False, False, "FA2 forward, head_dim 128: B2 H8 N4096 D128 non-causal"),
     "d128_3c": (2, 8, 4096, 128, True, False, "FA2 forward, head_dim 128: B2 H8 N4096 D128 causal"),
+    "sk20": (1, 20, 4096, 64, False, False,
+             "FA2 forward on a 2.16-wave grid (320 units on 148 SMs), stream-K schedule: B1 H20 N4096 D64 non-causal"),
 }
 
 
