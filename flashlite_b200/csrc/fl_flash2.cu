@@ -450,10 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         m_ref = m_new;
       }
       l *= alpha;
-      if (j > 0) {
-        // P V of the previous tile must be done before its P columns are
-        // rewritten and before O is rescaled.
-        if (!warp_wait(bar_pv(i), (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+      // P V of the previous tile must be done before its P columns are
+      // rewritten and before O is rescaled.
+      auto wait_pv_rescale = [&]() -> bool {
+        if (j == 0) return true;
+        if (!warp_wait(bar_pv(i), (j - 1) & 1, abort_flag, p.err)) return false;
         tc_fence_after();
         if (t == 0) FL_TRACE_EV(16 + i, j);
         if (__any_sync(0xffffffffu, need)) {
@@ -466,7 +467,15 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
             tmem_st32(tO + h * 32, o);
           }
         }
-      }
+        return true;
+      };
+      // Split-KV CTAs (head_dim 64) compute the step's exponentials before
+      // this wait and store P after it, so the wait overlaps them: config 2
+      // 322 -> 340 TF/s, config 2 causal 154 -> 164. In the two-tile
+      // instantiations the same order makes ptxas spill (216 bytes reloaded
+      // per step) and costs 3-9 %, so they wait first.
+      constexpr bool kExpFirst = kSplit && HD == 64;
+      if (!kExpFirst && !wait_pv_rescale()) { ok = false; break; }
       const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
       // p = 2^(s*scale - m_use): packed fp32x2 FMA for the argument, MUFU ex2,
       // fp16x2 pack for the PV operand; l sums the unrounded p in four
@@ -475,9 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       const float2 nm2 = make_float2(-m_use, -m_use);
       float2 lsum[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
+      uint32_t pk[kBN / 2];
 #pragma unroll
       for (int q = 0; q < kBN / 32; ++q) {
-        uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int c = q * 32 + 2 * e;
@@ -488,9 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
                                 ? exp2_poly2(x)
                                 : make_float2(ex2_approx(x.x), ex2_approx(x.y));
           lsum[e & 3] = __fadd2_rn(lsum[e & 3], pp);
-          pk[e] = pack_f16x2(pp.x, pp.y);
+          pk[q * 16 + e] = pack_f16x2(pp.x, pp.y);
         }
-        tmem_st16(tP + q * 16, pk);
+        if (!kExpFirst) tmem_st16(tP + q * 16, *reinterpret_cast<const uint32_t(*)[16]>(&pk[q * 16]));
         // Tile 1 starts when tile 0 is three quarters through its first KV
         // tile (128-key tiles; half-way with 64-key tiles): measured ~1 %
         // faster than half-way on the config-3 shapes, same output bits.
@@ -512,6 +521,12 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
         const float xm = fmaf(mx, scl, -m_use);
         const float pm = (mxp >= mxm) ? exp2_poly2(make_float2(xm, xm)).x : ex2_approx(xm);
         l += __half2float(__float2half_rn(pm)) - pm;
+      }
+      if (kExpFirst) {
+        if (!wait_pv_rescale()) { ok = false; break; }
+#pragma unroll
+        for (int q = 0; q < kBN / 32; ++q)
+          tmem_st16(tP + q * 16, *reinterpret_cast<const uint32_t(*)[16]>(&pk[q * 16]));
       }
       tmem_st_wait();
       tc_fence_before();
