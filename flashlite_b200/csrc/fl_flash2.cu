@@ -627,14 +627,14 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
       }
     } else {
       const int row = q_start + t;
-      if (active && row < p.nq && (do_out || (p.first && my_nkv == 0 && ok))) {
+      if (active && (do_out || (p.first && my_nkv == 0 && ok))) {  // warp-uniform
+        const bool valid = row < p.nq;
         // ln(sum_j exp(s_j*scale)) = (m_ref + log2(l)) * ln(2)
         const float lse_blk = (l > 0.0f) ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
-        float* orow = p.o_acc + (static_cast<long long>(bh) * p.nq + row) * kD;
         float* lrow = p.lse + static_cast<long long>(bh) * p.nq + row;
         float w_old = 0.0f, w_new = 1.0f, lse_out = lse_blk;
         if (!p.first) {
-          const float lse_old = *lrow;
+          const float lse_old = valid ? *lrow : -INFINITY;
           const float mx = fmaxf(lse_old, lse_blk);
           if (mx == -INFINITY) {
             w_old = 0.0f; w_new = 0.0f; lse_out = -INFINITY;
@@ -648,23 +648,70 @@ __global__ void __launch_bounds__(kThreads, 1) flash2_fwd_kernel(const __grid_co
           w_new = 0.0f;
         }
         const float wn = w_new * inv_l;
+        if (do_out) {
+          // Coalesced read-modify-write of the fp32 state. Each warp stages its
+          // 32 rows in its quarter of this tile's Q buffer (free: every S MMA
+          // of the tile completed before its last P V), kCols columns per
+          // pass, 16-byte chunk c of row r at chunk c ^ (r % kCh) so that
+          // neither the row-wise writes nor the column-wise reads conflict,
+          // then reads and writes 32 / kCh whole rows per instruction.
+          constexpr int kCols = kQTileBytes / 4 / (32 * 4);  // 32 (D = 64) or 64 (D = 128)
+          constexpr int kCh = kCols / 4;                     // 16-byte chunks per staged row
+          constexpr int kRowsPer = 32 / kCh;                 // rows per warp instruction
+          float4* stg = reinterpret_cast<float4*>(smem + kSmemQ + i * kQTileBytes + (warp & 3) * (kQTileBytes / 4));
+          const int row0 = q_start + (warp & 3) * 32;  // the warp's first row
+          constexpr int kIt = 32 / kRowsPer;       // row groups per pass
+          constexpr int kPre = kD == 64 ? 2 : 1;   // passes whose old state is loaded at once
+          const int c = lane & (kCh - 1);
 #pragma unroll
-        for (int c = 0; c < kD / 4; ++c) {
-          float4 r;
-          const float o0 = do_out ? __uint_as_float(o[4 * c + 0]) : 0.0f;
-          const float o1 = do_out ? __uint_as_float(o[4 * c + 1]) : 0.0f;
-          const float o2 = do_out ? __uint_as_float(o[4 * c + 2]) : 0.0f;
-          const float o3 = do_out ? __uint_as_float(o[4 * c + 3]) : 0.0f;
-          if (p.first) {
-            r = make_float4(o0 * wn, o1 * wn, o2 * wn, o3 * wn);
-          } else {
-            const float4 prev = reinterpret_cast<const float4*>(orow)[c];
-            r = make_float4(prev.x * w_old + o0 * wn, prev.y * w_old + o1 * wn,
-                            prev.z * w_old + o2 * wn, prev.w * w_old + o3 * wn);
+          for (int hb = 0; hb < kD / kCols; hb += kPre) {
+            // All loads of the old state first, so they are in flight together
+            // (and overlap the staging below) instead of one per row group.
+            float4 prev[kPre][kIt];
+#pragma unroll
+            for (int h2 = 0; h2 < kPre; ++h2)
+#pragma unroll
+              for (int k = 0; k < kIt; ++k) {
+                const int r = k * kRowsPer + lane / kCh;
+                prev[h2][k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (!p.first && row0 + r < p.nq)
+                  prev[h2][k] = reinterpret_cast<const float4*>(
+                      p.o_acc + (static_cast<long long>(bh) * p.nq + row0 + r) * kD + (hb + h2) * kCols)[c];
+              }
+#pragma unroll
+            for (int h2 = 0; h2 < kPre; ++h2) {
+              const int hf = hb + h2;
+#pragma unroll
+              for (int cc = 0; cc < kCh; ++cc) {
+                const int e = hf * kCols + 4 * cc;
+                stg[lane * kCh + (cc ^ (lane & (kCh - 1)))] =
+                    make_float4(__uint_as_float(o[e]) * wn, __uint_as_float(o[e + 1]) * wn,
+                                __uint_as_float(o[e + 2]) * wn, __uint_as_float(o[e + 3]) * wn);
+              }
+              __syncwarp();
+#pragma unroll
+              for (int k = 0; k < kIt; ++k) {
+                const int r = k * kRowsPer + lane / kCh;
+                const float wo = __shfl_sync(0xffffffffu, w_old, r);
+                const float4 v = stg[r * kCh + (c ^ (r & (kCh - 1)))];
+                if (row0 + r < p.nq) {
+                  const float4 pv = prev[h2][k];
+                  float4 out = v;
+                  if (!p.first) out = make_float4(pv.x * wo + v.x, pv.y * wo + v.y, pv.z * wo + v.z, pv.w * wo + v.w);
+                  reinterpret_cast<float4*>(p.o_acc + (static_cast<long long>(bh) * p.nq + row0 + r) * kD +
+                                            hf * kCols)[c] = out;
+                }
+              }
+              __syncwarp();
+            }
           }
-          reinterpret_cast<float4*>(orow)[c] = r;
+        } else if (valid) {
+          // no key visible to this tile (first block only): the state starts at zero
+          float4* orow = reinterpret_cast<float4*>(p.o_acc + (static_cast<long long>(bh) * p.nq + row) * kD);
+#pragma unroll
+          for (int c = 0; c < kD / 4; ++c) orow[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        *lrow = lse_out;
+        if (valid) *lrow = lse_out;
       }
     }
   }
