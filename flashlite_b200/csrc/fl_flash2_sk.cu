@@ -730,7 +730,11 @@ namespace {
 
 // Workspace of one (device, stream): launches on a stream run in order, so
 // one launch at a time uses it; launches on other streams have their own.
-// Created on first use (never while its stream is being captured) and kept.
+// Created on first use (never while its stream is being captured) and kept,
+// for at most kMaxSkWorkspaces streams per device: a caller that makes a new
+// stream per request must not grow device memory without bound, so further
+// streams run the one-unit-per-CTA schedule.
+constexpr int kMaxSkWorkspaces = 8;
 struct SkWorkspace {
   float* ws = nullptr;
   unsigned* cnt = nullptr;
@@ -794,7 +798,15 @@ cudaError_t launch_flash2_sk(Flash2Params prm, long long units, cudaStream_t str
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(sk_mutex());
-    SkWorkspace& w = sk_workspaces()[{dev, reinterpret_cast<uintptr_t>(stream)}];
+    auto& cache = sk_workspaces();
+    const std::pair<int, uintptr_t> key{dev, reinterpret_cast<uintptr_t>(stream)};
+    auto it = cache.find(key);
+    if (it == cache.end() || it->second.ws == nullptr) {
+      int on_dev = 0;  // workspaces that hold memory on this device
+      for (const auto& kv : cache) on_dev += (kv.first.first == dev && kv.second.ws != nullptr) ? 1 : 0;
+      if (on_dev >= kMaxSkWorkspaces) return cudaSuccess;  // the other schedule
+    }
+    SkWorkspace& w = cache[key];
     if (w.ws == nullptr || w.ws_floats < ws_floats || w.cnt_words < cnt_words) {
       cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
       if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {

@@ -44,8 +44,9 @@ typedef enum fl_status {
  * wave idle may run the stream-K schedule; the first such call on a stream
  * allocates that stream's 19.7 MB workspace (cudaMalloc, kept until exit;
  * never while the stream is being captured: the call then runs the other
- * schedule). FL_STREAMK=0 in the environment turns the schedule off. The
- * same holds for fl_flash2_fwd_ex.
+ * schedule). At most 8 streams per device get one; calls on further streams
+ * run the other schedule. FL_STREAMK=0 in the environment turns the schedule
+ * off. The same holds for fl_flash2_fwd_ex.
  */
 int fl_flash2_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t H,
                   int64_t N, int64_t D, float sm_scale, int is_causal, void* stream);

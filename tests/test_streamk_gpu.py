@@ -9,7 +9,7 @@ tiles (a unit with one tile), the LSE output, shapes it would not pick run in
 the forced mode (FL_STREAMK=2, in a subprocess: BASELINE config 3, tails of a
 few steps per CTA, units that are never cut, units without a second tile),
 repeatability, graph capture (with and without a workspace for the capturing
-stream) and concurrent streams. Same tolerance as
+stream), concurrent streams and the cap on cached workspaces. Same tolerance as
 forward_flash2: max-abs <= 2e-3, mean-abs <= 2e-4 against fp32 attention.
 """
 import os
@@ -163,3 +163,27 @@ def test_streamk_forced_small_tails(cuda):
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert "forced stream-K ok" in r.stdout
+
+
+def test_streamk_workspaces_are_capped(cuda):
+    """A caller that makes a new stream per request: at most 8 streams per
+    device keep a stream-K workspace (19.7 MB each); calls on further streams
+    run the one-unit-per-CTA schedule. Every result stays correct and the
+    library's device memory stays bounded."""
+    B, H, N = 1, 20, 4096
+    q, k, v = orc.make_qkv(B, H, N, 64, seed=21)
+    ref = orc.attention_fp32(q, k, v, 0.125, False)
+    qd, kd, vd = (t.to(cuda) for t in (q, k, v))
+    outs = [torch.empty_like(qd) for _ in range(12)]
+    streams = [torch.cuda.Stream(cuda) for _ in range(12)]
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(cuda)[0]
+    for s, o in zip(streams, outs):
+        with torch.cuda.stream(s):
+            fa.forward_flash2(qd, kd, vd, 0.125, False, out=o)
+    torch.cuda.synchronize()
+    grown = free0 - torch.cuda.mem_get_info(cuda)[0]
+    assert fa.device_error() == 0
+    assert grown <= 8 * 20 * 2**20 + (4 << 20), f"device memory grew by {grown / 2**20:.1f} MiB"
+    for i, o in enumerate(outs):
+        _check(o.cpu(), ref, f"stream {i}")
