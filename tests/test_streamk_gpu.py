@@ -5,7 +5,8 @@ than SMs, whose last wave would leave SMs idle, run as stream-K: each CTA
 takes an equal share of the concatenated KV steps, and a unit cut between
 two CTAs is merged by whichever piece finishes last. Covered: shapes the cost
 model sends there, ragged key and query lengths, an odd number of query
-tiles (a unit with one tile), the LSE output, shapes it would not pick run in
+tiles (a unit with one tile), the LSE output, the [B, N, H, D] layout, shapes
+it would not pick run in
 the forced mode (FL_STREAMK=2, in a subprocess: BASELINE config 3, tails of a
 few steps per CTA, units that are never cut, units without a second tile),
 repeatability, graph capture (with and without a workspace for the capturing
@@ -187,3 +188,17 @@ def test_streamk_workspaces_are_capped(cuda):
     assert grown <= 8 * 20 * 2**20 + (4 << 20), f"device memory grew by {grown / 2**20:.1f} MiB"
     for i, o in enumerate(outs):
         _check(o.cpu(), ref, f"stream {i}")
+
+
+def test_streamk_bnhd_layout(cuda):
+    """The [B, N, H, D] layout on a stream-K grid gives the [B, H, N, D] bits
+    (same cut points; only the tensor maps' strides differ), LSE included."""
+    B, H, N = 1, 20, 4096
+    q, k, v = (t.to(cuda) for t in orc.make_qkv(B, H, N, 64, seed=23))
+    ref, lse_ref = fa.forward_flash2_ex(q, k, v, 0.125, False, return_lse=True)
+    qt, kt, vt = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+    out, lse = fa.forward_flash2_ex(qt, kt, vt, 0.125, False, return_lse=True, layout="bnhd")
+    torch.cuda.synchronize()
+    assert fa.device_error() == 0
+    assert torch.equal(out.transpose(1, 2), ref)
+    assert torch.equal(lse, lse_ref)
