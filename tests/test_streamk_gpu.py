@@ -6,11 +6,11 @@ takes an equal share of the concatenated KV steps, and a unit cut between
 two CTAs is merged by whichever piece finishes last. Covered: shapes the cost
 model sends there, ragged key and query lengths, an odd number of query
 tiles (a unit with one tile), the LSE output, the [B, N, H, D] layout, shapes
-it would not pick run in
-the forced mode (FL_STREAMK=2, in a subprocess: BASELINE config 3, tails of a
-few steps per CTA, units that are never cut, units without a second tile),
-repeatability, graph capture (with and without a workspace for the capturing
-stream), concurrent streams and the cap on cached workspaces. Same tolerance as
+it would not pick run in the forced mode (FL_STREAMK=2, in a subprocess:
+BASELINE config 3, tails of a few steps per CTA, units that are never cut,
+units without a second tile), repeatability, graph capture (with and without
+a workspace for the capturing stream), concurrent streams and the cap on
+cached workspaces. Same tolerance as
 forward_flash2: max-abs <= 2e-3, mean-abs <= 2e-4 against fp32 attention.
 """
 import os
